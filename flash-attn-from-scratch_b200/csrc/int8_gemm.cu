@@ -1,0 +1,106 @@
+// int8_gemm.cu — C-ABI entry points of the tcgen05 kind::i8 GEMM with fused dequant.
+//
+// Restates kernels/int8_gemm/int8_gemm.py:33-90 (int8_gemm_dequant_kernel):
+//   acc[m,n] = sum_k A[m,k] * B[k,n]          int32, exact
+//   C[m,n]   = fp16(fp32(acc) * sa[m] * sb[n])  evaluated left to right (:84), RN conversion
+// on sm_100a: the int32 accumulator lives in tensor memory and is dequantised straight from
+// TMEM in the epilogue, so it never touches HBM.
+#include "gemm_sm100.cuh"
+#include "lk_abi.h"
+
+namespace lk {
+namespace {
+
+using gemm::Epi;
+using gemm::Kind;
+
+int make_int8_maps(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, bool b_mn, int M, int N, int K,
+                   int BN, CUtensorMap* ta, CUtensorMap* tb) {
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)lda};
+    const uint32_t box[2] = {128, 128};
+    if (int st = make_tmap(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  if (b_mn) {
+    // B row-major [K, N]: innermost N.  Box = 128 N-bytes x 128 k-rows.
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)ldb};
+    const uint32_t box[2] = {128, 128};
+    return make_tmap(tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    // B row-major [N, K]: innermost K.  Box = 128 K-bytes x BN rows.
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)ldb};
+    const uint32_t box[2] = {128, (uint32_t)BN};
+    return make_tmap(tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+}
+
+template <Epi kEpi>
+int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout, const float* sa,
+             const float* sb, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return LK_ERR_INVALID_ARG;
+  if (b_layout != 0 && b_layout != 1) return LK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return LK_OK;
+  if (!A || !B || !C) return LK_ERR_INVALID_ARG;
+  if (kEpi == Epi::DequantF16 && (!sa || !sb)) return LK_ERR_INVALID_ARG;
+  if (K == 0) return LK_ERR_INVALID_ARG;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return LK_ERR_INVALID_ARG;
+  const bool b_mn = (b_layout == 0);
+  if (lda < K || ldc < N) return LK_ERR_INVALID_ARG;
+  if (b_mn ? (ldb < N) : (ldb < K)) return LK_ERR_INVALID_ARG;
+  if (lda % 16 || ldb % 16) return LK_ERR_ALIGNMENT;
+  if (int st = bind_stream(stream)) return st;
+
+  const int num_sms = sm_count();
+  const int tiles_m = (int)((M + gemm::kBM - 1) / gemm::kBM);
+  // Wide tiles halve operand traffic per MMA; narrow ones only when wide ones cannot fill the GPU.
+  const int tiles_n256 = (int)((N + 255) / 256);
+  const bool narrow = (int64_t)tiles_m * tiles_n256 < num_sms && N > 128;
+  const int BN = narrow ? 128 : 256;
+  const int tiles_n = (int)((N + BN - 1) / BN);
+
+  CUtensorMap ta, tb;
+  if (int st = make_int8_maps(A, lda, B, ldb, b_mn, (int)M, (int)N, (int)K, BN, &ta, &tb)) return st;
+
+  gemm::Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_m = tiles_m;
+  p.tiles_n = tiles_n;
+  p.num_tiles = tiles_m * tiles_n;
+  p.C = C;
+  p.ldc = ldc;
+  p.sa = sa;
+  p.sb = sb;
+  p.rstd = nullptr;
+
+  int err;
+  if (BN == 256) {
+    err = b_mn ? gemm::launch<Kind::I8, 256, true, kEpi>(ta, tb, p, num_sms, stream)
+               : gemm::launch<Kind::I8, 256, false, kEpi>(ta, tb, p, num_sms, stream);
+  } else {
+    err = b_mn ? gemm::launch<Kind::I8, 128, true, kEpi>(ta, tb, p, num_sms, stream)
+               : gemm::launch<Kind::I8, 128, false, kEpi>(ta, tb, p, num_sms, stream);
+  }
+  return cuda_status((cudaError_t)err);
+}
+
+}  // namespace
+}  // namespace lk
+
+extern "C" int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                                    const float* scale_a, const float* scale_b, void* C, int64_t ldc, int64_t M,
+                                    int64_t N, int64_t K, void* stream) {
+  return lk::run_int8<lk::gemm::Epi::DequantF16>(A, lda, B, ldb, b_layout, scale_a, scale_b, C, ldc, M, N, K,
+                                                 static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout, int32_t* C,
+                                int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream) {
+  return lk::run_int8<lk::gemm::Epi::RawI32>(A, lda, B, ldb, b_layout, nullptr, nullptr, C, ldc, M, N, K,
+                                             static_cast<cudaStream_t>(stream));
+}

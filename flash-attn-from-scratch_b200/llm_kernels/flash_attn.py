@@ -1,0 +1,75 @@
+"""Flash-attention forward on sm_100a (tcgen05 + TMEM + TMA).
+
+Drop-in for the reference's ``kernels/flash_attn/flash_attn_fwd.py:131-156``
+(``flash_attn_forward``), which dispatched to a non-causal (:6-64) or causal (:67-128) Triton
+kernel.  Same arguments and defaults; as a superset it also accepts bf16, ragged M/N (no
+tile-multiple requirement) and an optional ``softmax_scale``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._common import dtype_code, ptr, require, require_cuda, stream_for
+
+__all__ = ["flash_attn_forward"]
+
+
+def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_scale=None):
+    """``O = softmax(Q K^T * scale [+ causal mask]) V`` for ``[B, H, M, D]`` tensors.
+
+    Args:
+        q : [B, H, M, D] fp16 / bf16, CUDA (any strides with a contiguous last dim)
+        k, v : [B, H, N, D], same dtype and device
+        causal : mask keys n > m (top-left aligned, flash_attn_fwd.py:118)
+        block_m, block_n : accepted for signature compatibility; the sm_100a kernel uses
+            its own 128-row tiles and handles any M, N.
+        softmax_scale : defaults to D**-0.5 (flash_attn_fwd.py:50)
+
+    Returns:
+        out : like ``q`` (``torch.empty_like(q)``, flash_attn_fwd.py:136)
+    """
+    require(isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor) and isinstance(v, torch.Tensor), "q, k, v must be tensors")
+    require(q.dtype in (torch.float16, torch.bfloat16) and q.is_cuda, "q must be a CUDA fp16/bf16 tensor")
+    require(k.dtype == q.dtype and v.dtype == q.dtype, "q, k, v must share a dtype")
+    dev = require_cuda("flash_attn_forward", q, k, v)
+    require(q.dim() == 4 and k.dim() == 4 and v.dim() == 4, "q, k, v must be [B, H, seq, D]")
+    for name, val in (("block_m", block_m), ("block_n", block_n)):
+        require(isinstance(val, int) and val > 0, f"{name} must be a positive int")
+    B, H, M, D = q.shape
+    N = k.shape[2]
+    require(k.shape == (B, H, N, D) and v.shape == (B, H, N, D), "k and v must be [B, H, N, D] matching q")
+    require(0 < D <= 128, f"head dim {D} not supported (1..128)")
+    scale = float(softmax_scale) if softmax_scale is not None else float(D) ** -0.5
+    if D not in (64, 128):
+        # The tcgen05 kernels are built for D = 64 and 128; other head dims are zero-padded
+        # (zero columns add nothing to Q K^T, and the padded output columns are dropped).
+        Dp = 64 if D < 64 else 128
+        pad = lambda t: torch.nn.functional.pad(t, (0, Dp - D))
+        out = flash_attn_forward(pad(q), pad(k), pad(v), causal, block_m, block_n, softmax_scale=scale)
+        res = torch.empty_like(q)
+        res.copy_(out[..., :D])
+        return res
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k.stride(-1) != 1:
+        k = k.contiguous()
+    if v.stride(-1) != 1:
+        v = v.contiguous()
+    out = torch.empty_like(q)
+    if out.stride(-1) != 1:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    if out.numel() == 0:
+        return out
+    require(N > 0, "flash_attn_forward: need at least one key")
+    s = stream_for(dev)
+    _lib.call(
+        "lk_flash_attn_fwd",
+        ptr(q), ptr(k), ptr(v), ptr(out), dtype_code(q.dtype),
+        B, H, M, N, D,
+        _lib.i64_array(q.stride()), _lib.i64_array(k.stride()),
+        _lib.i64_array(v.stride()), _lib.i64_array(out.stride()),
+        1 if causal else 0, scale, s,
+    )
+    return out

@@ -1,0 +1,148 @@
+/*
+ * llm_kernels_b200.h — C ABI of the sm_100a (B200) llm_kernels inference op set.
+ *
+ * Every entry point takes plain device pointers, 64-bit sizes/strides (in ELEMENTS), a dtype
+ * code where the op is type-generic, and a cudaStream_t passed as `void*` (NULL = legacy
+ * default stream).  Calls are asynchronous on that stream, never synchronise, never allocate
+ * device memory, and return an lk_status code.  Argument errors are detected on the host
+ * before anything is launched.
+ *
+ * Device-side failures (a pipeline wait that ran out of time) do not trap: the kernel records
+ * the failure in a device status word and unwinds.  lk_device_status() reads that word
+ * (it synchronises the device) and lk_clear_device_status() resets it.
+ *
+ * Outputs are caller-allocated.  The reference allocated them inside its wrappers
+ * (kernels/flash_attn/flash_attn_fwd.py:136, kernels/int8_gemm/int8_gemm.py:122,
+ * csrc/bindings.cpp:53); the Python layer of this library does the same on top of this ABI.
+ */
+#ifndef LLM_KERNELS_B200_H
+#define LLM_KERNELS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LK_API __attribute__((visibility("default")))
+#else
+#define LK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------ */
+typedef enum {
+  LK_OK = 0,
+  LK_ERR_INVALID_ARG = 1,   /* null pointer, bad shape, mismatched sizes                        */
+  LK_ERR_UNSUPPORTED = 2,   /* dtype / head dim / layout this build does not implement           */
+  LK_ERR_CUDA = 3,          /* a CUDA runtime or driver call failed (see lk_last_cuda_error)    */
+  LK_ERR_TIMEOUT = 4,       /* a device-side pipeline wait ran out (from lk_device_status)      */
+  LK_ERR_ALIGNMENT = 5      /* pointer or stride not 16-byte aligned where TMA needs it          */
+} lk_status;
+
+/* ---- dtype codes ------------------------------------------------------------------------- */
+typedef enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 2, LK_I8 = 3, LK_I32 = 4 } lk_dtype;
+
+/* Human-readable name of a status code (static string). */
+LK_API const char* lk_status_string(int status);
+
+/* The cudaError_t of the last LK_ERR_CUDA returned on this host thread (0 if none). */
+LK_API int lk_last_cuda_error(void);
+
+/* ABI version: (major << 16) | minor. */
+LK_API int lk_version(void);
+
+/* Makes `device` the current device for this library's calls on the calling host thread.
+ * Entry points given a non-NULL stream bind to that stream's device themselves; calls on the
+ * legacy default stream (NULL) run on the device set here (default 0). */
+LK_API int lk_set_device(int device);
+
+/* Synchronises the current device, then copies its status word into out4 (may be NULL):
+ * out4[0] = lk_status of the first device failure (0 = none), out4[1] = failure site id,
+ * out4[2] = blockIdx.x, out4[3] = threadIdx.x of the thread that recorded it.
+ * Returns out4[0] (or LK_ERR_CUDA). */
+LK_API int lk_device_status(int* out4);
+
+/* Resets the current device's status word to 0 (synchronous). */
+LK_API int lk_clear_device_status(void);
+
+/* ---- quantize_symmetric ------------------------------------------------------------------ *
+ * Replaces kernels/int8_gemm/int8_gemm.py:146-161 (quantize_symmetric).
+ * Per-row symmetric absmax quantisation of x[rows, cols] (last dim contiguous, row stride
+ * x_ld elements; x_dtype LK_F32 / LK_F16 / LK_BF16):
+ *     scale[r] = fp32(max_c |x[r,c]|) / 127          (IEEE division, NaN-propagating max)
+ *     q[r,c]   = clamp(rint(x[r,c] / scale[r]), -128, 127)  (IEEE division, ties to even;
+ *                a NaN quotient gives 0, as the reference's CPU cast does)
+ * q is int8 with row stride q_ld; scale is fp32[rows]. */
+LK_API int lk_quantize_symmetric(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t x_ld,
+                          int8_t* q, int64_t q_ld, float* scale, void* stream);
+
+/* ---- int8 GEMM with fused dequant --------------------------------------------------------- *
+ * Replaces kernels/int8_gemm/int8_gemm.py:98-138 (int8_gemm_dequant_fwd) and its kernel
+ * kernels/int8_gemm/int8_gemm.py:33-90.
+ *     acc[m,n] = sum_k A[m,k] * B(k,n)              (exact int32)
+ *     C[m,n]   = fp16( (fp32(acc[m,n]) * scale_a[m]) * scale_b[n] )   (two RN multiplies)
+ * A is int8 [M,K] row-major with row stride lda.  b_layout selects B's storage:
+ *     0 = [K,N] row-major, row stride ldb (the reference's layout, int8_gemm.py:100),
+ *     1 = [N,K] row-major, row stride ldb (a weight's natural layout; no transpose copy).
+ * C is fp16 [M,N] row-major with row stride ldc.
+ * Requirements: K % 16 == 0; lda, ldb, ldc and the base pointers 16-byte aligned. */
+LK_API int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                         const float* scale_a, const float* scale_b, void* C, int64_t ldc,
+                         int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Same GEMM, writing the raw int32 accumulator (C int32 [M,N], row stride ldc) instead of the
+ * dequantised fp16.  Exists so the accumulator can be checked bit for bit. */
+LK_API int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                     int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- flash attention forward ------------------------------------------------------------ *
+ * Replaces kernels/flash_attn/flash_attn_fwd.py:131-156 (flash_attn_forward) and its two
+ * kernels (flash_attn_fwd.py:6-64 non-causal, :67-128 causal).
+ *     O[b,h,m,:] = sum_n softmax_n(scale * <Q[b,h,m,:], K[b,h,n,:]>) V[b,h,n,:]
+ * causal != 0 masks keys n > m (top-left aligned, flash_attn_fwd.py:118).
+ * dtype LK_F16 or LK_BF16 for all four tensors; head dim D in {64, 128}; M, N >= 1 arbitrary
+ * (no tile-multiple requirement).  Strides are in elements, 4 per tensor in (b, h, row, d)
+ * order; the d stride must be 1 and the others multiples of 8 elements.  softmax_scale <= 0
+ * selects D^-0.5 (the reference's hard-coded scale, flash_attn_fwd.py:50). */
+LK_API int lk_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype,
+                      int64_t B, int64_t H, int64_t M, int64_t N, int64_t D,
+                      const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides,
+                      int causal, float softmax_scale, void* stream);
+
+/* ---- fused RMSNorm + Linear --------------------------------------------------------------- *
+ * Replaces csrc/fused_rmsnorm_linear.cu:105-120 (launch_fused_rmsnorm_linear) behind
+ * csrc/bindings.cpp:26-67, and the fallback kernels/fused_rmsnorm_linear/fused_ops.py:27-37:
+ *     y[r,:] = rsqrt(mean_k x[r,k]^2 + eps) * ( (x[r,:] * w_norm) @ w_lin^T )
+ *
+ * lk_rmsnorm_linear_fold writes w_fold[n,k] = dtype(w_lin[n,k] * w_norm[k]) — the RMSNorm gain
+ * folded into the weight, a weight-side transform done once per weight version (w_norm may be
+ * LK_F32, LK_F16 or LK_BF16; w_lin and w_fold are `dtype`).
+ *
+ * lk_rmsnorm_linear runs two kernels on `stream`: a row kernel that writes
+ * row_rstd[r] = rsqrt(mean_k x[r,k]^2 + eps) (fp32 scratch, `rows` floats), and one tcgen05
+ * GEMM x @ w_fold^T whose epilogue multiplies row r by row_rstd[r].  The GEMM is launched as a
+ * programmatic dependent of the row kernel: only its epilogue waits for row_rstd.
+ * dtype LK_F16 or LK_BF16 for x, w_fold and y.  x [rows, d_in] and y [rows, d_out] are
+ * row-major with row strides x_ld, y_ld (elements); w_fold is [d_out, d_in] contiguous.
+ * Requirements: d_in % 8 == 0, x_ld % 8 == 0, 16-byte aligned base pointers. */
+LK_API int lk_rmsnorm_linear_fold(const void* w_norm, int w_norm_dtype, const void* w_lin, void* w_fold,
+                                  int dtype, int64_t d_in, int64_t d_out, void* stream);
+LK_API int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld,
+                             int dtype, int64_t rows, int64_t d_in, int64_t d_out, float eps,
+                             float* row_rstd, void* stream);
+
+/* One-call form with the reference launcher's argument list (csrc/fused_rmsnorm_linear.cu:105:
+ * X, W_norm, W_lin, Y, eps, B, D_in, D_out, stream) plus the dtype and two caller-owned scratch
+ * buffers: w_fold (D_out * D_in elements of dtype, rewritten on every call) and row_rstd
+ * (B floats).  W_norm has the same dtype as X. */
+LK_API int lk_fused_rmsnorm_linear(const void* X, const void* W_norm, const void* W_lin, void* Y,
+                                   float eps, int64_t B, int64_t D_in, int64_t D_out, int dtype,
+                                   void* w_fold, float* row_rstd, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLM_KERNELS_B200_H */

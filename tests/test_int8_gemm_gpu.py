@@ -1,0 +1,100 @@
+"""int8 GEMM on the GPU vs the oracle: bit-exact int32 accumulator and bit-exact fp16
+dequantised output, both B layouts, ragged shapes, and the 4096^3 config."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import llm_kernels
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand_i8(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+
+
+SHAPES = [(128, 256, 128), (256, 512, 384), (100, 72, 96), (1, 16, 16), (129, 257, 144), (300, 1000, 512),
+          (1024, 1024, 1024), (64, 4096, 4096), (17, 40, 50), (3, 5, 7)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+def test_int32_accumulator_bit_exact(M, N, K, layout):
+    A = _rand_i8((M, K), 1 + M)
+    B = _rand_i8((K, N) if layout == "kn" else (N, K), 2 + N)
+    C = llm_kernels.int8_gemm_i32(A.cuda(), B.cuda(), layout)
+    ref = oracle.int8_gemm_i32(A.numpy(), B.numpy(), layout)
+    np.testing.assert_array_equal(C.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (100, 72, 96), (512, 512, 512), (333, 160, 256)])
+def test_dequant_fp16_bit_exact(M, N, K):
+    g = torch.Generator().manual_seed(7 + M)
+    A_fp = torch.randn(M, K, generator=g).to(torch.float16)
+    B_fp = torch.randn(K, N, generator=g).to(torch.float16)
+    A_q, sa = llm_kernels.quantize_symmetric(A_fp.cuda())
+    B_q, sb = llm_kernels.quantize_symmetric(B_fp.T.contiguous().cuda())
+    B_kn = B_q.T.contiguous()
+    C = llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb)
+    ref = oracle.int8_gemm_dequant(A_q.cpu().numpy(), B_kn.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy(), "kn")
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+    C2 = llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb)
+    np.testing.assert_array_equal(C2.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def test_golden_vectors_from_reference_kernel():
+    g = np.load(os.path.join(GOLDEN, "int8_gemm.npz"))
+    for tag in ("sq", "rag"):
+        A = torch.from_numpy(g[f"{tag}_A"]).cuda()
+        B = torch.from_numpy(g[f"{tag}_B_kn"]).cuda()
+        sa = torch.from_numpy(g[f"{tag}_sa"]).cuda()
+        sb = torch.from_numpy(g[f"{tag}_sb"]).cuda()
+        C = llm_kernels.int8_gemm_dequant_fwd(A, B, sa, sb)
+        np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), g[f"{tag}_C"].view(np.uint16))
+
+
+def test_full_size_4096_cubed():
+    """Config 3: M=N=K=4096, inputs quantised per row.  The accumulator of a row block is
+    checked bit-exactly against the oracle and the whole matrix through an exact checksum
+    (sum over n of C[m,n] == A[m,:] . rowsum(B)), computed in int64."""
+    g = torch.Generator().manual_seed(2)
+    A_fp = torch.randn(4096, 4096, generator=g).to(torch.float16)
+    B_fp = torch.randn(4096, 4096, generator=g).to(torch.float16)  # [N, K]
+    A_q, sa = llm_kernels.quantize_symmetric(A_fp.cuda())
+    B_q, sb = llm_kernels.quantize_symmetric(B_fp.cuda())
+    B_kn = B_q.T.contiguous()
+    acc = llm_kernels.int8_gemm_i32(A_q, B_kn, "kn")
+    rows = slice(1024, 1280)
+    ref = oracle.int8_gemm_i32(A_q[rows].cpu().numpy(), B_q.cpu().numpy(), "nk")
+    np.testing.assert_array_equal(acc[rows].cpu().numpy(), ref)
+    lhs = acc.to(torch.int64).sum(1)
+    rhs = (A_q.to(torch.int64) * B_q.to(torch.int64).sum(0)[None, :]).sum(1)
+    assert torch.equal(lhs, rhs)
+    C = llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb)
+    refC = oracle.dequant_f16(acc.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy())
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), refC.view(np.uint16))
+
+
+def test_int8_linear_module_matches_oracle():
+    torch.manual_seed(6)
+    layer = llm_kernels.Int8Linear(256, 384)
+    w = torch.randn(384, 256, dtype=torch.float16).cuda()
+    layer.quantize_weights(w)
+    x = torch.randn(40, 256, dtype=torch.float16).cuda()
+    y = layer(x)
+    xq, sx = oracle.quantize_symmetric(x.cpu())
+    ref = oracle.int8_gemm_dequant(xq, layer.w_q.cpu().numpy(), sx, layer.scale_w.cpu().numpy(), "nk")
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def test_zero_and_degenerate_shapes():
+    A = torch.zeros(0, 64, dtype=torch.int8, device="cuda")
+    B = torch.zeros(64, 32, dtype=torch.int8, device="cuda")
+    out = llm_kernels.int8_gemm_dequant_fwd(A, B, torch.ones(0, device="cuda"), torch.ones(32, device="cuda"))
+    assert out.shape == (0, 32) and out.dtype == torch.float16

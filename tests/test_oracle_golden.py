@@ -1,0 +1,89 @@
+"""The oracle against golden vectors produced by the reference's own code (CPU only).
+
+tests/golden/make_golden.py ran the reference here: quantize_symmetric and
+_rmsnorm_linear_ref directly, the int8 GEMM and flash-attention Triton kernels under
+TRITON_INTERPRET=1.  Passing these pins the oracle to the reference before it is used to
+check the sm_100a kernels.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN, name + ".npz"))
+
+
+def _bf16(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", ["f16", "f32", "bf16", "f16_wide", "f32_special"])
+def test_quantize_bit_exact_vs_reference(case):
+    g = _load("quantize")
+    x = g[f"{case}_x"]
+    x = _bf16(x) if case == "bf16" else torch.from_numpy(x)
+    q, s = oracle.quantize_symmetric(x)
+    np.testing.assert_array_equal(q, g[f"{case}_q"])
+    ref_s = g[f"{case}_scale"]
+    assert np.array_equal(np.isnan(s), np.isnan(ref_s))
+    ok = ~np.isnan(ref_s)
+    assert np.array_equal(s[ok].view(np.uint32), ref_s[ok].view(np.uint32))
+
+
+@pytest.mark.parametrize("tag", ["sq", "rag"])
+def test_int8_gemm_dequant_bit_exact_vs_reference_kernel(tag):
+    g = _load("int8_gemm")
+    C = oracle.int8_gemm_dequant(g[f"{tag}_A"], g[f"{tag}_B_kn"], g[f"{tag}_sa"], g[f"{tag}_sb"], "kn")
+    np.testing.assert_array_equal(C.view(np.uint16), g[f"{tag}_C"].view(np.uint16))
+
+
+@pytest.mark.parametrize("tag", ["sq", "rag"])
+def test_int8_accumulator_layouts_agree(tag):
+    g = _load("int8_gemm")
+    A, B = g[f"{tag}_A"], g[f"{tag}_B_kn"]
+    c_kn = oracle.int8_gemm_i32(A, B, "kn")
+    c_nk = oracle.int8_gemm_i32(A, np.ascontiguousarray(B.T), "nk")
+    c_np = (A.astype(np.int64) @ B.astype(np.int64))
+    np.testing.assert_array_equal(c_kn, c_np)
+    np.testing.assert_array_equal(c_nk, c_np)
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_attention_fp32_vs_reference_kernel(causal):
+    g = _load("flash_attn")
+    q, k, v = (torch.from_numpy(g[n]) for n in ("q", "k", "v"))
+    ref = torch.from_numpy(g[f"out_causal{causal}"]).float()
+    out = oracle.attention_fp32(q, k, v, causal=bool(causal))
+    # the reference kernel stores fp16 and feeds PV with fp16 probabilities
+    assert (out - ref).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("tag", ["f32", "f16"])
+def test_rmsnorm_linear_vs_reference(tag):
+    g = _load("rmsnorm_linear")
+    x, wn, wl = (torch.from_numpy(g[f"{tag}_{n}"]) for n in ("x", "w_norm", "w_lin"))
+    y = oracle.rmsnorm_linear_ref(x, wn, wl, 1e-6, round_to_input_dtype=(tag == "f16"))
+    ref = torch.from_numpy(g[f"{tag}_y"]).float()
+    rel = (y - ref).abs().max() / ref.abs().max()
+    assert rel.item() < (1e-6 if tag == "f32" else 2e-3)
+
+
+def test_golden_vectors_reject_a_planted_rounding_mistake():
+    """A quantiser that rounds half away from zero (a plausible bug) must fail the golden
+    codes on the ties row, so the fixtures really discriminate the rounding mode."""
+    g = _load("quantize")
+    x = g["f32_special_x"].astype(np.float32)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        scale = np.abs(x).max(-1) / np.float32(127)
+        t = x / scale[:, None]
+        wrong = np.where(np.isnan(t), 0, np.clip(np.sign(t) * np.floor(np.abs(t) + 0.5), -128, 127)).astype(np.int8)
+    assert not np.array_equal(wrong[4], g["f32_special_q"][4])
+    q, _ = oracle.quantize_symmetric(torch.from_numpy(x))
+    np.testing.assert_array_equal(q, g["f32_special_q"])

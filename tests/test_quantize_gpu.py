@@ -1,0 +1,81 @@
+"""quantize_symmetric on the GPU vs the oracle: bit-exact int8 codes and fp32 scales."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import llm_kernels
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(x: torch.Tensor):
+    q, s = llm_kernels.quantize_symmetric(x)
+    assert q.dtype == torch.int8 and s.dtype == torch.float32
+    assert q.shape == x.shape and s.shape == x.shape[:-1]
+    rq, rs = oracle.quantize_symmetric(x.cpu())
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    gs = s.cpu().numpy()
+    assert np.array_equal(np.isnan(gs), np.isnan(rs))
+    ok = ~np.isnan(rs)
+    assert np.array_equal(gs[ok].view(np.uint32), rs[ok].view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(1, 8), (37, 200), (64, 4096), (5, 8192), (3, 12000), (7, 33), (2, 50000)])
+def test_quantize_matches_oracle(dtype, shape):
+    g = torch.Generator().manual_seed(hash((str(dtype), shape)) & 0xFFFF)
+    x = (torch.randn(*shape, generator=g) * 2.5).to(dtype).cuda()
+    _check(x)
+
+
+def test_quantize_golden_vectors():
+    g = np.load(os.path.join(GOLDEN, "quantize.npz"))
+    for case in ("f16", "f32", "bf16", "f16_wide", "f32_special"):
+        x = g[f"{case}_x"]
+        xt = torch.from_numpy(x.astype(np.int16)).view(torch.bfloat16) if case == "bf16" else torch.from_numpy(x)
+        q, s = llm_kernels.quantize_symmetric(xt.cuda())
+        np.testing.assert_array_equal(q.cpu().numpy(), g[f"{case}_q"])
+        ref_s = g[f"{case}_scale"]
+        gs = s.cpu().numpy()
+        assert np.array_equal(np.isnan(gs), np.isnan(ref_s))
+        ok = ~np.isnan(ref_s)
+        assert np.array_equal(gs[ok].view(np.uint32), ref_s[ok].view(np.uint32))
+
+
+def test_quantize_special_rows():
+    x = torch.randn(8, 64)
+    x[0] = 0.0
+    x[1, 7] = float("inf")
+    x[2, 9] = float("nan")
+    x[3] = -0.0
+    x[4, :] = 1e-45
+    x[5, 0] = -float("inf")
+    for dt in (torch.float32, torch.float16, torch.bfloat16):
+        _check(x.to(dt).cuda())
+
+
+def test_quantize_strided_rows_and_leading_dims():
+    base = torch.randn(16, 300, dtype=torch.float16).cuda()
+    _check(base[:, :256])  # row stride 300 != cols
+    x3 = torch.randn(2, 5, 96, dtype=torch.bfloat16).cuda()
+    q, s = llm_kernels.quantize_symmetric(x3)
+    rq, rs = oracle.quantize_symmetric(x3.cpu())
+    assert q.shape == (2, 5, 96) and s.shape == (2, 5)
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+
+
+def test_quantize_full_size_4096sq():
+    """The int8 GEMM config's operand (4096 x 4096 fp16): bit-exact against the oracle."""
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(4096, 4096, generator=g).to(torch.float16).cuda()
+    _check(x)
+
+
+def test_quantize_empty_rows():
+    q, s = llm_kernels.quantize_symmetric(torch.empty(0, 64, device="cuda", dtype=torch.float16))
+    assert q.shape == (0, 64) and s.shape == (0,)
