@@ -1,8 +1,448 @@
-// flash_attn.cu — placeholder until the tcgen05 attention kernel lands.
-#include "lk_abi.h"
+// flash_attn.cu — flash-attention forward on sm_100a: tcgen05 MMAs into tensor memory, TMA
+// K/V streaming, online softmax in registers.
+//
+// Restates the reference's online-softmax forward (kernels/flash_attn/flash_attn_fwd.py:47-64
+// non-causal, :108-128 causal):  for each key block, S = Q K^T * scale, running row max m and
+// row sum l, O = alpha * O + P V with P cast to the input dtype (:61), final O / l (:63).
+// Causal masking keeps key n for query m iff n <= m (top-left, :118) and skips key blocks
+// entirely above the diagonal (:112).
+//
+// CTA = one (batch, head) and 256 query rows held as two 128-row tiles (t = 0, 1) that
+// ping-pong on the tensor core.  10 warps:
+//   warps 0-3  softmax for tile 0 (thread = one query row = one TMEM lane)
+//   warps 4-7  softmax for tile 1
+//   warp  8    TMA producer: Q0/Q1 once, then K_0, V_0, K_1, V_1, ... through a ring of
+//              128-row stages (128B swizzle)
+//   warp  9    TMEM owner + single-thread MMA issuer
+// Tensor memory (512 columns): S_t = cols [128t, 128t+128) fp32; P_t (bf16/f16 pairs) is
+// written over the first 64 columns of S_t; O_t = cols [256 + D*t, 256 + D*(t+1)) fp32.
+// MMA issue order per key block j:  S0(j), PV1(j-1), S1(j), PV0(j)  — so while softmax of
+// tile 0 runs on S0(j) the tensor core computes PV1(j-1) and S1(j), and vice versa.  Since
+// tcgen05 MMAs from one thread execute in order, the commit that publishes S_t(j) also
+// guarantees PV_t(j-1) finished: the softmax warps may rescale O_t right away.
+// Rescaling is lazy: the running max used for exp2 only moves when the block max exceeds it
+// by more than 8 (log2 units), so P <= 256 and O is rarely touched.
+// Every mbarrier wait is bounded; on failure all roles unwind and TMEM is freed.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
-extern "C" int lk_flash_attn_fwd(const void*, const void*, const void*, void*, int, int64_t, int64_t, int64_t,
-                                 int64_t, int64_t, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
-                                 int, float, void*) {
-  return LK_ERR_UNSUPPORTED;
+#include <atomic>
+
+#include "lk_abi.h"
+#include "lk_sm100.cuh"
+
+namespace lk {
+namespace fa {
+
+constexpr int kThreads = 320;
+constexpr int kTileM = 128;   // query rows per tile
+constexpr int kBlockN = 128;  // keys per block
+constexpr int kRingBytes = 128 * 1024;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+enum Site : int {
+  kSiteLoadQ = 201,
+  kSiteLoadEmpty = 202,
+  kSiteMmaQ = 203,
+  kSiteMmaKV = 204,
+  kSiteMmaP = 205,
+  kSiteSoftS = 206,
+  kSiteSoftO = 207,
+  kSiteTeardown = 208,
+};
+
+struct Params {
+  int B, H, M, N;
+  int num_qblocks;  // ceil(M / 256)
+  int causal;
+  float scale_log2;  // softmax scale * log2(e)
+  void* o;
+  int64_t o_sb, o_sh, o_sm;  // element strides of O (d stride is 1)
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int kQBoxes = D / 64;                 // 64-element (128 B) boxes per row
+  static constexpr int kTileBytes = kTileM * D * 2;      // one 128-row tile of Q, K or V
+  static constexpr int kStages = kRingBytes / kTileBytes;  // 4 (D=128) / 8 (D=64)
+  static constexpr int kSmemBytes = 2 * kTileBytes + kRingBytes + 1024 + 512;
+  static constexpr int kOCol0 = 256;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <int D, bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<D>;
+  constexpr int S = C::kStages;
+  constexpr uint32_t kIdescS = make_idesc(1, kBf16 ? 1 : 0, kBf16 ? 1 : 0, 0, 0, kTileM, kBlockN);
+  constexpr uint32_t kIdescO = make_idesc(1, kBf16 ? 1 : 0, kBf16 ? 1 : 0, 0, 1, kTileM, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                          // [2][kTileBytes]
+  uint8_t* sRing = smem + 2 * C::kTileBytes;   // [S][kTileBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kRingBytes);
+  uint64_t* q_full = bars;             // [1]
+  uint64_t* kv_full = bars + 1;        // [S]
+  uint64_t* kv_empty = kv_full + S;    // [S]
+  uint64_t* s_full = kv_empty + S;     // [2]
+  uint64_t* p_full = s_full + 2;       // [2]  128 arrivals each
+  uint64_t* o_full = p_full + 2;       // [2]
+  uint64_t* drain = o_full + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+
+  // Heavy-first ordering: the first B*H CTAs take the last (longest, when causal) q-block
+  // of every head.
+  const int BH = p.B * p.H;
+  const int qb = p.num_qblocks - 1 - (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qb * 2 * kTileM;
+  const int nkb = (p.N + kBlockN - 1) / kBlockN;
+  int nb[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qs = q0 + t * kTileM;
+    if (qs >= p.M) {
+      nb[t] = 0;
+    } else if (p.causal) {
+      const int last = (qs + kTileM - 1) / kBlockN;  // diagonal block (qs is a multiple of 128)
+      nb[t] = min(nkb, last + 1);
+    } else {
+      nb[t] = nkb;
+    }
+  }
+  const int J = max(nb[0], nb[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], kTileM);
+      mbar_init(&o_full[t], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      const int ntiles = nb[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
+      for (int t = 0; t < ntiles; ++t)
+        for (int x = 0; x < C::kQBoxes; ++x)
+          tma_load_4d(sQ + t * C::kTileBytes + x * (kTileM * 128), &tmQ, q_full, 64 * x, q0 + t * kTileM, h, b);
+      int issued = 0;
+      for (int i = 0; i < 2 * J && ok; ++i) {
+        const int slot = i % S;
+        const uint32_t par = ((i / S) & 1) ^ 1u;
+        if (!mbar_wait(&kv_empty[slot], par, kSiteLoadEmpty)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[slot], C::kTileBytes);
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+        const int row = (i >> 1) * kBlockN;
+        uint8_t* dst = sRing + slot * C::kTileBytes;
+        for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, h, b);
+        issued = i + 1;
+      }
+      // Teardown: every copy issued must land before the CTA can exit.
+      mbar_wait(q_full, 0, kSiteTeardown);
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+        mbar_wait(&kv_full[i % S], (i / S) & 1, kSiteTeardown);
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, kSiteMmaQ);
+      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + C::kTileBytes)};
+      auto item_addr = [&](int i) { return smem_u32(sRing + (i % S) * C::kTileBytes); };
+      auto wait_item = [&](int i) { return mbar_wait(&kv_full[i % S], (i / S) & 1, kSiteMmaKV); };
+      auto release_item = [&](int i) { tc_commit(&kv_empty[i % S]); };
+      // S_t = Q_t K_j^T : K-major A (Q) and B (K), K = D in steps of 16.
+      auto issue_s = [&](int t, int j) {
+        const uint32_t kb = item_addr(2 * j);
+        const uint32_t d_tmem = tmem + t * kBlockN;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * (kTileM * 128) + (ks & 3) * 32;
+          mma_f16_ss(d_tmem, sdesc_sw128(q_addr[t] + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), kIdescS,
+                     ks > 0);
+        }
+        tc_commit(&s_full[t]);
+      };
+      // O_t (+)= P_t V_j : A = P_t from TMEM (cols of S_t), B = V_j MN-major (D contiguous).
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = item_addr(2 * j + 1);
+        const uint32_t o_tmem = tmem + C::kOCol0 + t * D;
+        const uint32_t p_tmem = tmem + t * kBlockN;
+#pragma unroll
+        for (int ks = 0; ks < kBlockN / 16; ++ks) {
+          mma_f16_ts(o_tmem, p_tmem + ks * 8, sdesc_sw128(vb + ks * 16 * 128, kTileM * 128, 1024), kIdescO,
+                     (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        if (j == nb[t] - 1) tc_commit(&o_full[t]);
+      };
+      for (int j = 0; j < J && ok; ++j) {
+        if (!wait_item(2 * j)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (j < nb[0]) issue_s(0, j);
+        if (j >= 1 && j - 1 < nb[1]) {
+          if (!mbar_wait(&p_full[1], (j - 1) & 1, kSiteMmaP) || !wait_item(2 * j - 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(1, j - 1);
+          release_item(2 * j - 1);  // V_{j-1}: its last reader was PV1(j-1)
+        }
+        if (j < nb[1]) issue_s(1, j);
+        release_item(2 * j);  // K_j
+        if (j < nb[0]) {
+          if (!mbar_wait(&p_full[0], j & 1, kSiteMmaP) || !wait_item(2 * j + 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j >= nb[1]) release_item(2 * j + 1);  // tile 1 does not use V_j
+        } else if (j >= nb[1]) {
+          release_item(2 * j + 1);
+        }
+      }
+      if (ok && nb[1] > 0 && nb[1] == J) {
+        const int j = J - 1;
+        if (mbar_wait(&p_full[1], j & 1, kSiteMmaP) && wait_item(2 * j + 1)) {
+          tc_fence_after();
+          issue_pv(1, j);
+          release_item(2 * j + 1);
+        }
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0, kSiteTeardown);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 0-7)
+    const int t = warp >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // row inside the tile == TMEM lane
+    const int m = q0 + t * kTileM + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_tmem = tmem + lane_off + t * kBlockN;
+    const uint32_t o_tmem = tmem + lane_off + C::kOCol0 + t * D;
+    const int lim = p.causal ? min(m, p.N - 1) : (p.N - 1);  // last visible key of this row
+    float m_used = -INFINITY;  // running max actually used for exp2 (log2-scaled units)
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb[t]; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, kSiteSoftS)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[kBlockN];
+#pragma unroll
+      for (int c = 0; c < kBlockN / 32; ++c) tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_wait_ld();
+      const int n0 = j * kBlockN;
+      if (n0 + kBlockN - 1 > lim) {
+#pragma unroll
+        for (int c = 0; c < kBlockN; ++c)
+          if (n0 + c > lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
+#pragma unroll
+      for (int c = 4; c < kBlockN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float m_new = mx * p.scale_log2;
+      const bool need = m_new > m_used + kRescaleThreshold;
+      const bool warp_rescale = __any_sync(0xffffffffu, need) && j > 0;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2(m_used - m_new);  // 0 on the first block (m_used = -inf)
+        m_used = m_new;
+      }
+      l *= alpha;
+      const float neg = -m_used;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBlockN / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(fmaf(__uint_as_float(sr[c * 32 + 2 * e]), p.scale_log2, neg));
+          const float p1 = ex2(fmaf(__uint_as_float(sr[c * 32 + 2 * e + 1]), p.scale_log2, neg));
+          rs0 += p0;
+          rs1 += p1;
+          pk[e] = pack2<kBf16>(p0, p1);
+        }
+        tmem_st16(s_tmem + c * 16, pk);
+      }
+      l += rs0 + rs1;
+      if (warp_rescale) {
+        // O_t's last writer PV_t(j-1) completed before S_t(j) was published, and PV_t(j) is
+        // not issued before p_full below.  Done after P so the S registers are free.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(o_tmem + c * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(o_tmem + c * 32, ov);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    // Epilogue: O / l -> global.
+    if (ok && nb[t] > 0) {
+      if (mbar_wait(&o_full[t], 0, kSiteSoftO)) {
+        tc_fence_after();
+        const float inv = 1.f / l;
+        const bool row_ok = m < p.M;
+        uint16_t* orow = static_cast<uint16_t*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)m * p.o_sm;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(o_tmem + c * 32, ov);
+          tmem_wait_ld();
+          if (row_ok) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack2<kBf16>(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv);
+              w.y = pack2<kBf16>(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv);
+              w.z = pack2<kBf16>(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv);
+              w.w = pack2<kBf16>(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv);
+              reinterpret_cast<uint4*>(orow + c * 32)[q] = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, 512);
+}
+
+template <int D, bool kBf16>
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const Params& p, cudaStream_t s) {
+  using C = Cfg<D>;
+  auto kern = fa_fwd_kernel<D, kBf16>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured.fetch_or(bit);
+  }
+  const int64_t grid = (int64_t)p.num_qblocks * p.B * p.H;
+  kern<<<(unsigned)grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, p);
+  return check_launch();
+}
+
+int make_map(CUtensorMap* map, bool bf16, const void* base, int64_t B, int64_t H, int64_t S, int64_t D,
+             const int64_t* st) {
+  if (st[3] != 1) return LK_ERR_INVALID_ARG;
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return make_tmap(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims,
+                   strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace fa
+}  // namespace lk
+
+extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t B,
+                                 int64_t H, int64_t M, int64_t N, int64_t D, const int64_t* q_strides,
+                                 const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                 int causal, float softmax_scale, void* stream) {
+  using namespace lk;
+  if (B < 0 || H < 0 || M < 0 || N < 0) return LK_ERR_INVALID_ARG;
+  if (B == 0 || H == 0 || M == 0) return LK_OK;
+  if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides || N == 0)
+    return LK_ERR_INVALID_ARG;
+  if (dtype != LK_BF16 && dtype != LK_F16) return LK_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return LK_ERR_UNSUPPORTED;
+  if (M > (1 << 30) || N > (1 << 30) || B * H > (1 << 30)) return LK_ERR_INVALID_ARG;
+  if (o_strides[3] != 1 || ((uintptr_t)o & 15)) return LK_ERR_ALIGNMENT;
+  for (int i = 0; i < 3; ++i)
+    if (o_strides[i] % 8) return LK_ERR_ALIGNMENT;
+  const int64_t nqb = (M + 2 * fa::kTileM - 1) / (2 * fa::kTileM);
+  if (nqb * B * H > 0x7FFFFFFF) return LK_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int st = bind_stream(s)) return st;
+  const bool bf16 = dtype == LK_BF16;
+  CUtensorMap tq, tk, tv;
+  if (int st = fa::make_map(&tq, bf16, q, B, H, M, D, q_strides)) return st;
+  if (int st = fa::make_map(&tk, bf16, k, B, H, N, D, k_strides)) return st;
+  if (int st = fa::make_map(&tv, bf16, v, B, H, N, D, v_strides)) return st;
+  fa::Params p{};
+  p.B = (int)B;
+  p.H = (int)H;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.num_qblocks = (int)nqb;
+  p.causal = causal ? 1 : 0;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = o;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_sm = o_strides[2];
+  if (D == 128) return bf16 ? fa::launch<128, true>(tq, tk, tv, p, s) : fa::launch<128, false>(tq, tk, tv, p, s);
+  return bf16 ? fa::launch<64, true>(tq, tk, tv, p, s) : fa::launch<64, false>(tq, tk, tv, p, s);
 }

@@ -1,0 +1,113 @@
+"""Flash-attention forward on the GPU vs the fp32 oracle softmax(Q K^T * scale) V.
+
+Tolerance (the north star's): max |O - O_fp32| <= 1e-2, where O_fp32 is computed in fp32
+on the CPU from the same fp16/bf16 inputs.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import llm_kernels
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2
+
+
+def _qkv(B, H, M, N, D, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, M, D, generator=g).to(dtype)
+    k = torch.randn(B, H, N, D, generator=g).to(dtype)
+    v = torch.randn(B, H, N, D, generator=g).to(dtype)
+    return q, k, v
+
+
+def _err(out, ref):
+    return (out.float().cpu() - ref).abs().max().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("M,N", [(128, 128), (256, 256), (512, 512), (384, 384), (1024, 1024)])
+def test_matches_fp32_oracle(dtype, D, causal, M, N):
+    q, k, v = _qkv(1, 2, M, N, D, dtype, M * 7 + D)
+    out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    assert out.shape == q.shape and out.dtype == dtype
+    ref = oracle.attention_fp32(q, k, v, causal)
+    assert _err(out, ref) <= ATOL
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("M,N", [(1, 1), (5, 77), (100, 100), (200, 333), (333, 200), (129, 257), (700, 64), (64, 700)])
+def test_ragged_and_rectangular(causal, M, N):
+    q, k, v = _qkv(2, 3, M, N, 128, torch.bfloat16, M + 13 * N)
+    out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    ref = oracle.attention_fp32(q, k, v, causal)
+    assert _err(out, ref) <= ATOL
+
+
+def test_golden_vectors_from_reference_kernel():
+    g = np.load(os.path.join(GOLDEN, "flash_attn.npz"))
+    q, k, v = (torch.from_numpy(g[n]).cuda() for n in ("q", "k", "v"))
+    for causal in (0, 1):
+        out = llm_kernels.flash_attn_forward(q, k, v, causal=bool(causal))
+        ref = torch.from_numpy(g[f"out_causal{causal}"]).float()
+        assert _err(out, ref) <= ATOL
+
+
+def test_strided_views_and_head_dim_padding():
+    # [B, T, H, D] storage viewed as [B, H, T, D] (experiments/attention_ablation.py:171-177)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 300, 4, 3, 64, generator=g).to(torch.float16).cuda()
+    q, k, v = (x[:, :, :, i].transpose(1, 2) for i in range(3))
+    out = llm_kernels.flash_attn_forward(q, k, v, causal=True)
+    ref = oracle.attention_fp32(q, k, v, True)
+    assert _err(out, ref) <= ATOL
+    q32, k32, v32 = _qkv(1, 2, 96, 96, 32, torch.float16, 5)
+    out = llm_kernels.flash_attn_forward(q32.cuda(), k32.cuda(), v32.cuda(), causal=False)
+    assert out.shape == (1, 2, 96, 32)
+    assert _err(out, oracle.attention_fp32(q32, k32, v32, False)) <= ATOL
+
+
+def test_softmax_scale_argument():
+    q, k, v = _qkv(1, 2, 256, 256, 128, torch.bfloat16, 8)
+    out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=True, softmax_scale=0.3)
+    assert _err(out, oracle.attention_fp32(q, k, v, True, scale=0.3)) <= ATOL
+
+
+def test_large_logits_trigger_rescaling():
+    """Scaled-up queries give row maxima that grow along the sequence: exercises the lazy
+    O rescaling path (running max moves by > 8 in log2 units)."""
+    q, k, v = _qkv(1, 2, 512, 1024, 128, torch.bfloat16, 9)
+    ramp = torch.linspace(0.1, 4.0, 1024)[None, None, :, None]
+    k = (k.float() * ramp).to(torch.bfloat16)
+    q = (q.float() * 3).to(torch.bfloat16)
+    for causal in (False, True):
+        out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+        assert _err(out, oracle.attention_fp32(q, k, v, causal)) <= ATOL
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_config2_full_size_subset_of_heads(causal):
+    """Config 2 (B4 H32 N4096 D128 bf16, seed 1): the whole problem runs on the GPU; four
+    (b, h) slices are checked against the fp32 oracle on the CPU."""
+    q, k, v = _qkv(4, 32, 4096, 4096, 128, torch.bfloat16, 1)
+    out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal).cpu()
+    for b, h in ((0, 0), (1, 7), (2, 19), (3, 31)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        ref = oracle.attention_fp32(q[sl], k[sl], v[sl], causal)
+        assert _err(out[sl], ref) <= ATOL
+
+
+def test_module_wrapper_and_repr():
+    attn = llm_kernels.FlashAttention(causal=False, block_m=128, block_n=64)
+    assert "causal=False" in repr(attn)
+    q, k, v = _qkv(1, 4, 128, 128, 64, torch.float16, 2)
+    out = attn(q.cuda(), k.cuda(), v.cuda())
+    assert _err(out, oracle.attention_fp32(q, k, v, False)) <= ATOL

@@ -1,0 +1,114 @@
+"""Fused RMSNorm + Linear on the GPU vs the fp32 oracle (the reference's PyTorch path,
+kernels/fused_rmsnorm_linear/fused_ops.py:27-37).
+
+Tolerance (the north star's): relative error <= 1e-2, measured as
+max|y - y_ref| / max|y_ref| over the whole output.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import llm_kernels
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+
+
+def _rel(y, ref):
+    return ((y.float().cpu() - ref).abs().max() / ref.abs().max()).item()
+
+
+def _inputs(rows, d_in, d_out, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, d_in, generator=g)
+    w_norm = 1 + 0.1 * torch.randn(d_in, generator=g)
+    w_lin = torch.randn(d_out, d_in, generator=g) / d_in ** 0.5
+    return x.to(dtype), w_norm.to(dtype), w_lin.to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,d_in,d_out", [(64, 512, 512), (512, 4096, 4096), (1, 256, 128), (130, 264, 200),
+                                             (1000, 1024, 3000), (257, 4096, 384)])
+def test_matches_fp32_oracle(dtype, rows, d_in, d_out):
+    x, wn, wl = _inputs(rows, d_in, d_out, dtype, rows + d_out)
+    y = llm_kernels.fused_rmsnorm_linear(x.cuda(), wn.cuda(), wl.cuda(), 1e-6)
+    assert y.shape == (rows, d_out) and y.dtype == dtype
+    ref = oracle.rmsnorm_linear_ref(x, wn, wl, 1e-6)
+    assert _rel(y, ref) <= REL_TOL
+
+
+def test_config1_fp32_inputs_run_in_bf16():
+    """Config 1 (x [512,4096] fp32 N(0,1), w_norm 1+0.1N, w_lin N/64, seed 0): the GPU runs the
+    same values in bf16 and fp16; both stay within tolerance of the fp32 oracle on the fp32
+    inputs."""
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(512, 4096, generator=g)
+    w_norm = 1 + 0.1 * torch.randn(4096, generator=g)
+    w_lin = torch.randn(4096, 4096, generator=g) / 64
+    ref = oracle.rmsnorm_linear_ref(x, w_norm, w_lin, 1e-6)
+    for dt in (torch.bfloat16, torch.float16):
+        y = llm_kernels.fused_rmsnorm_linear(x.to(dt).cuda(), w_norm.cuda(), w_lin.to(dt).cuda(), 1e-6)
+        assert _rel(y, ref) <= REL_TOL
+
+
+def test_golden_vectors():
+    g = np.load(os.path.join(GOLDEN, "rmsnorm_linear.npz"))
+    x, wn, wl = (torch.from_numpy(g[f"f16_{n}"]) for n in ("x", "w_norm", "w_lin"))
+    y = llm_kernels.fused_rmsnorm_linear(x.cuda(), wn.cuda(), wl.cuda(), 1e-6)
+    ref = torch.from_numpy(g["f16_y"]).float()
+    assert _rel(y, ref) <= REL_TOL
+
+
+def test_module_and_weight_updates_invalidate_fold_cache():
+    torch.manual_seed(4)
+    mod = llm_kernels.FusedRMSNormLinear(256, 192).cuda()
+    x = torch.randn(33, 256, dtype=torch.float16).cuda()
+    y0 = mod(x)
+    ref0 = oracle.rmsnorm_linear_ref(x, mod.w_norm, mod.w_lin)
+    assert _rel(y0, ref0) <= REL_TOL
+    with torch.no_grad():
+        mod.w_norm.mul_(2.0)  # in-place update bumps _version: the folded weight must be rebuilt
+        mod.w_lin[:5].zero_()
+    y1 = mod(x)
+    ref1 = oracle.rmsnorm_linear_ref(x, mod.w_norm, mod.w_lin)
+    assert _rel(y1, ref1) <= REL_TOL
+    sd = mod.state_dict()
+    assert set(sd) == {"w_norm", "w_lin"} and sd["w_lin"].shape == (192, 256)
+
+
+def test_leading_dims_and_strided_rows():
+    x, wn, wl = _inputs(24, 128, 64, torch.bfloat16, 5)
+    x3 = x.reshape(2, 12, 128).cuda()
+    y = llm_kernels.fused_rmsnorm_linear(x3, wn.cuda(), wl.cuda())
+    assert y.shape == (2, 12, 64)
+    ref = oracle.rmsnorm_linear_ref(x, wn, wl)
+    assert _rel(y.reshape(24, 64), ref) <= REL_TOL
+    big = torch.randn(24, 192, dtype=torch.bfloat16).cuda()
+    big[:, :128] = x.cuda()
+    y2 = llm_kernels.fused_rmsnorm_linear(big[:, :128], wn.cuda(), wl.cuda())
+    assert _rel(y2, ref) <= REL_TOL
+
+
+def test_one_call_abi_matches_two_step():
+    """lk_fused_rmsnorm_linear (the reference launcher's argument list) through the C ABI."""
+    from llm_kernels import _lib
+
+    x, wn, wl = _inputs(64, 512, 256, torch.float16, 9)
+    x, wn, wl = x.cuda(), wn.cuda(), wl.cuda()
+    y = torch.empty(64, 256, dtype=torch.float16, device="cuda")
+    wf = torch.empty_like(wl)
+    rstd = torch.empty(64, dtype=torch.float32, device="cuda")
+    _lib.set_device(0)
+    _lib.call("lk_fused_rmsnorm_linear", x.data_ptr(), wn.data_ptr(), wl.data_ptr(), y.data_ptr(), 1e-6, 64, 512,
+              256, _lib.LK_F16, wf.data_ptr(), rstd.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = llm_kernels.fused_rmsnorm_linear(x, wn, wl)
+    assert torch.equal(y, ref)
+    exp = oracle.rmsnorm_linear_ref(x, wn, wl)
+    assert _rel(y, exp) <= REL_TOL
