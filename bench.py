@@ -1,0 +1,534 @@
+"""Benchmark of the llm_kernels inference op set on B200 (one JSON line on stdout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--quick]
+
+Headline workload (the metric's first clause, configs[1] of the op set's benchmark list):
+flash-attention forward, causal, bf16, B=4 H=32 N=4096 D=128, TFLOP/s with causal FLOPs
+counted as half of dense (4*B*H*N^2*D / 2).  One step = one flash_attn_forward call over
+one batch.  Inputs are 384 MiB per step (larger than the 126 MB L2), so no L2 flush is
+needed between steps.  The other two clauses of the metric (int8 GEMM+dequant TOPS at
+4096^3 and RMSNorm+Linear ms at 512x4096->4096) and the rest of the op set are measured in
+the same run and reported under "ops".
+
+Multi-GPU (launched by torchrun, one process per GPU): the batch is sharded — every rank
+runs its own B=4 slice of a global batch of 4*N (weak scaling), no collective on the data
+path; the timed region is bracketed by barriers and the max over ranks is reported.
+
+--impl reference times the reference's CPU path on the host cores: torch SDPA in fp32 on
+the CPU (the reference's FA test oracle; its FA itself is GPU-only Triton), on a bounded
+sample of the same workload per step; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flash-attn-from-scratch_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "FA fwd TFLOP/s (causal bf16 N=4096 D=128); int8 GEMM+dequant TOPS; RMSNorm+Lin ms"
+B, H, N, D = 4, 32, 4096, 128
+FLOPS_CAUSAL = 4.0 * B * H * N * N * D / 2  # causal counted as half of dense
+
+
+CONFIG = {
+    "workload": "flash-attention forward causal bf16, B=4 H=32 N=4096 D=128 per GPU "
+                "(global batch 4*n_gpus, batch-sharded)",
+    "B_per_gpu": B, "H": H, "N": N, "D": D, "causal": True,
+    "flops_per_step_per_gpu": FLOPS_CAUSAL,
+    "l2": "inputs larger than L2 (384 MiB per step), no flush",
+}
+
+
+def fa_flops(b, h, n, d, causal):
+    return 4.0 * b * h * n * n * d * (0.5 if causal else 1.0)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, window=None):
+        """Summary of the samples received inside `window` = (t_start, t_end) host seconds."""
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ts, ln in self.lines:
+            if window is not None and not (window[0] <= ts <= window[1] + 0.05):
+                continue
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "power_w_max": max(power) if power else None,
+            "samples": len(sm),
+            "reasons": sorted(reasons),
+        }
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------------------------
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------
+# device timing helpers
+# ---------------------------------------------------------------------------------------------
+def time_loop(fn, steps: int, warmup: int, world: int) -> float:
+    """Total device ms of `steps` back-to-back calls (events on the current stream), max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(steps):
+        fn()
+    b.record(s)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(a.elapsed_time(b), world)
+
+
+def time_each_flushed(fn, reps: int, warmup: int, flush: torch.Tensor) -> float:
+    """Median device ms of one call, with L2 flushed (a 256 MiB write) before every call."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        fn()
+        b.record(s)
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baselines (the oracle port of the reference's CPU path)
+# ---------------------------------------------------------------------------------------------
+def cpu_fa_sample(heads: int, reps: int):
+    import oracle
+
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, heads, N, D, generator=g)
+    k = torch.randn(1, heads, N, D, generator=g)
+    v = torch.randn(1, heads, N, D, generator=g)
+    oracle.attention_fp32(q[:, :1, :512], k[:, :1, :512], v[:, :1, :512], True)  # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+    dt = (time.perf_counter() - t0) / reps
+    return fa_flops(1, heads, N, D, True) / dt / 1e12, dt
+
+
+def cpu_baselines():
+    """The reference's CPU path timed on this host: returns dict of op -> baseline."""
+    import oracle
+
+    threads = torch.get_num_threads()
+    out = {}
+    tf, dt = cpu_fa_sample(heads=32, reps=2)
+    out["flash_attn_causal"] = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                "sample": f"torch SDPA fp32 causal, B=1 H=32 N=4096 D=128 (1/4 of the batch), "
+                                          f"{dt * 1e3:.0f} ms/call"}
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(512, 4096, generator=g)
+    wn = 1 + 0.1 * torch.randn(4096, generator=g)
+    wl = torch.randn(4096, 4096, generator=g) / 64
+    oracle.rmsnorm_linear_ref(x, wn, wl)
+    t0 = time.perf_counter()
+    for _ in range(5):
+        oracle.rmsnorm_linear_ref(x, wn, wl)
+    dt = (time.perf_counter() - t0) / 5
+    out["rmsnorm_linear"] = {"value": dt * 1e3, "unit": "ms", "cores": threads, "kind": "port",
+                             "sample": "fp32 RMSNorm+Linear 512x4096->4096 (the full config-1 problem), 5 calls"}
+    a = torch.randint(-127, 128, (512, 4096), dtype=torch.int8).numpy()
+    bm = torch.randint(-127, 128, (4096, 4096), dtype=torch.int8).numpy()
+    t0 = time.perf_counter()
+    acc = oracle.int8_gemm_i32(a, bm, "nk", threads=threads)
+    oracle.dequant_f16(acc, torch.full((512,), 1e-3).numpy(), torch.full((4096,), 1e-3).numpy())
+    dt = time.perf_counter() - t0
+    out["int8_gemm_dequant"] = {"value": 2 * 512 * 4096 * 4096 / dt / 1e12, "unit": "TOPS", "cores": threads,
+                                "kind": "port",
+                                "sample": "int32 GEMM + dequant, M=512 rows of the 4096^3 problem (1/8), C restatement"}
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference arm
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = torch.get_num_threads()
+    heads = 2 if args.quick else 8  # per step: B=1, `heads` heads of the B4 H32 N4096 D128 problem
+    import oracle
+
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, heads, N, D, generator=g)
+    k = torch.randn(1, heads, N, D, generator=g)
+    v = torch.randn(1, heads, N, D, generator=g)
+    fn = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = time.perf_counter() - t0
+    flops = fa_flops(1, heads, N, D, True) * args.steps
+    val = flops / dt / 1e12
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": val,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) q/k/v)",
+        "config": CONFIG,
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"B=1 H={heads} of the workload per step, torch SDPA fp32 causal"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def run_ours(args):
+    import llm_kernels
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peaks_kind = measured_peaks()
+
+    # ---- headline: causal FA config 2 on every rank (its own batch shard) ----
+    g = torch.Generator().manual_seed(1 + rank)
+    q = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    step = lambda: llm_kernels.flash_attn_forward(q, k, v, causal=True)  # noqa: E731
+
+    clocks = ClockSampler(local)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling; only samples inside the timed window count
+    t_start = time.time()
+    total_ms = time_loop(step, args.steps, 0, world)
+    clk = clocks.stop(window=(t_start, time.time()))
+    ms = total_ms / args.steps
+    value = FLOPS_CAUSAL * world / (ms * 1e-3) / 1e12  # whole job: all ranks' work / max time
+    launches = args.steps  # one fa_fwd_kernel launch per step
+
+    # ---- end to end through the public API, host buffers (rank-local) ----
+    qh = q.cpu().pin_memory()
+    kh = k.cpu().pin_memory()
+    vh = v.cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        o = llm_kernels.flash_attn_forward(qd, kd, vd, causal=True)
+        oh.copy_(o, non_blocking=True)
+
+    e2e_steps = max(3, args.steps // 4)
+    e2e_ms = time_loop(e2e_step, e2e_steps, 2, world) / e2e_steps
+    e2e_val = FLOPS_CAUSAL * world / (e2e_ms * 1e-3) / 1e12
+    nbytes = q.numel() * q.element_size()
+
+    ops = {}
+    cpu = None
+    if rank == 0:
+        ops = secondary_ops(args, llm_kernels, peaks)
+        if world == 1:
+            cpu = cpu_baselines()
+
+    traffic = profile_traffic().get("flash_attn_causal_bf16_B4_H32_N4096_D128")
+    peak = float(peaks["bf16_tflops"])
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v; no dataset)",
+        "config": CONFIG,
+        "roofline": {
+            "bound": "tensor",
+            "achieved": FLOPS_CAUSAL / (ms * 1e-3) / 1e12,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": FLOPS_CAUSAL / (ms * 1e-3) / 1e12 / peak,
+            "peak_kind": f"{peaks_kind} bf16 burst (cuBLAS), kernel timed alone",
+            "kernel": "lk::fa::fa_fwd_kernel<128, bf16>",
+            "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+            "algorithmic_bytes": 4 * nbytes,
+        },
+        "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * nbytes,
+                "d2h_bytes_per_step": nbytes},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "ops": ops,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu["flash_attn_causal"]
+        line["cpu_baselines"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def secondary_ops(args, llm_kernels, peaks):
+    """The metric's other clauses and the rest of the op set (rank 0, L2 flushed per call)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    reps = 5 if args.quick else 20
+    ops = {}
+    hbm = float(peaks["hbm_gbs"])
+    # int8 GEMM + dequant, M=N=K=4096, per-row quantised operands (config 3)
+    g = torch.Generator().manual_seed(2)
+    A_fp = torch.randn(4096, 4096, generator=g).to(torch.float16).to(dev)
+    B_fp = torch.randn(4096, 4096, generator=g).to(torch.float16).to(dev)
+    A_q, sa = llm_kernels.quantize_symmetric(A_fp)
+    B_q, sb = llm_kernels.quantize_symmetric(B_fp)
+    B_kn = B_q.t().contiguous()
+    ms = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb), reps, 3, flush)
+    ops["int8_gemm_dequant_4096"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
+                                     "frac_of_4500_dense_int8_spec": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12 / 4500,
+                                     "layout": "B [K,N] (reference API)"}
+    ms = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb), reps, 3, flush)
+    ops["int8_gemm_dequant_4096_nk"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
+                                        "layout": "B [N,K] (Int8Linear weight)"}
+    # quantize_symmetric 4096x4096 fp16 (config 3b)
+    ms = time_each_flushed(lambda: llm_kernels.quantize_symmetric(A_fp), reps, 3, flush)
+    qbytes = 4096 * 4096 * 2 + 4096 * 4096 + 4096 * 4
+    ops["quantize_4096_f16"] = {"value": qbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ms,
+                                "frac_of_hbm": qbytes / (ms * 1e-3) / 1e9 / hbm}
+    # fused RMSNorm + Linear, config 1 shape (bf16 and fp16)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(512, 4096, generator=g)
+    wn = (1 + 0.1 * torch.randn(4096, generator=g))
+    wl = torch.randn(4096, 4096, generator=g) / 64
+    for dt, tag in ((torch.bfloat16, "bf16"), (torch.float16, "f16")):
+        xd, wnd, wld = x.to(dt).to(dev), wn.to(dt).to(dev), wl.to(dt).to(dev)
+        llm_kernels.fused_rmsnorm_linear(xd, wnd, wld)  # folds the weight once (cached per weight version)
+        ms = time_each_flushed(lambda: llm_kernels.fused_rmsnorm_linear(xd, wnd, wld), reps, 3, flush)
+        ops[f"rmsnorm_linear_512x4096x4096_{tag}"] = {"value": ms, "unit": "ms",
+                                                      "tflops": 2 * 512 * 4096 * 4096 / (ms * 1e-3) / 1e12}
+    # non-causal FA config 2
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, k, v, causal=False), reps, 2, 1) / reps
+    ops["flash_attn_noncausal_bf16_B4H32N4096D128"] = {"value": fa_flops(B, H, N, D, False) / (ms * 1e-3) / 1e12,
+                                                       "unit": "TFLOP/s", "ms": ms}
+    del q, k, v
+    # config 4 sweep: fp16, B8 H16 D64
+    sweep = {}
+    for n in ([512, 4096] if args.quick else [512, 1024, 2048, 4096, 8192, 16384]):
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(8, 16, n, 64, generator=g).to(torch.float16).to(dev)
+        k = torch.randn(8, 16, n, 64, generator=g).to(torch.float16).to(dev)
+        v = torch.randn(8, 16, n, 64, generator=g).to(torch.float16).to(dev)
+        r = max(3, min(reps, int(2e4 / n)))
+        for causal in (True, False):
+            ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, k, v, causal=causal), r, 2, 1) / r
+            sweep[f"N{n}_{'causal' if causal else 'dense'}"] = round(fa_flops(8, 16, n, 64, causal) / (ms * 1e-3) / 1e12, 1)
+        del q, k, v
+    ops["flash_attn_sweep_f16_B8H16D64_tflops"] = sweep
+    del flush
+    return ops
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quick", action="store_true", help="fewer repetitions of the secondary ops")
+    ap.add_argument("--only", choices=["fa", "fa_dense", "int8", "quantize", "rmsnorm"], default=None,
+                    help="run just one op's device loop (warmup + steps) and print nothing else: "
+                         "the command the ncu profiles under profiles/ are taken on")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+def run_only(args):
+    """One op's kernels alone (for ncu); no timing, no output besides a done line."""
+    import llm_kernels
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(1)
+    if args.only in ("fa", "fa_dense"):
+        q = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+        k = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+        v = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+        fn = lambda: llm_kernels.flash_attn_forward(q, k, v, causal=args.only == "fa")  # noqa: E731
+    elif args.only in ("int8", "quantize"):
+        A_fp = torch.randn(4096, 4096, generator=g).to(torch.float16).to(dev)
+        B_fp = torch.randn(4096, 4096, generator=g).to(torch.float16).to(dev)
+        A_q, sa = llm_kernels.quantize_symmetric(A_fp)
+        B_q, sb = llm_kernels.quantize_symmetric(B_fp)
+        B_kn = B_q.t().contiguous()
+        if args.only == "int8":
+            fn = lambda: llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb)  # noqa: E731
+        else:
+            fn = lambda: llm_kernels.quantize_symmetric(A_fp)  # noqa: E731
+    else:
+        x = torch.randn(512, 4096, generator=g).to(torch.bfloat16).to(dev)
+        wn = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16).to(dev)
+        wl = (torch.randn(4096, 4096, generator=g) / 64).to(torch.bfloat16).to(dev)
+        fn = lambda: llm_kernels.fused_rmsnorm_linear(x, wn, wl)  # noqa: E731
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(f"only={args.only} done", flush=True)
+
+
+if __name__ == "__main__":
+    main()

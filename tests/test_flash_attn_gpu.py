@@ -19,6 +19,17 @@ pytestmark = pytest.mark.gpu
 ATOL = 1e-2
 
 
+def _err_scaled(out, ref):
+    """max |O - O_fp32| / max(1, |O_fp32|).
+
+    Used by the stress tests whose peaked softmax produces |O| > 2.5: there a bf16 output
+    cannot be within 1e-2 of the fp32 value at all (half an ulp of bf16 in [4, 8) is
+    0.0156), so the bound is 1e-2 absolute below |O| = 1 and 1e-2 relative above.  In fp16
+    the same cases stay below 3e-3 absolute."""
+    o = out.float().cpu()
+    return ((o - ref).abs() / ref.abs().clamp(min=1.0)).max().item()
+
+
 def _qkv(B, H, M, N, D, dtype, seed):
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, H, M, D, generator=g).to(dtype)
@@ -78,7 +89,10 @@ def test_strided_views_and_head_dim_padding():
 def test_softmax_scale_argument():
     q, k, v = _qkv(1, 2, 256, 256, 128, torch.bfloat16, 8)
     out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=True, softmax_scale=0.3)
-    assert _err(out, oracle.attention_fp32(q, k, v, True, scale=0.3)) <= ATOL
+    assert _err_scaled(out, oracle.attention_fp32(q, k, v, True, scale=0.3)) <= ATOL
+    q16, k16, v16 = (t.to(torch.float16) for t in (q, k, v))
+    out16 = llm_kernels.flash_attn_forward(q16.cuda(), k16.cuda(), v16.cuda(), causal=True, softmax_scale=0.3)
+    assert _err(out16, oracle.attention_fp32(q16, k16, v16, True, scale=0.3)) <= ATOL
 
 
 def test_large_logits_trigger_rescaling():
@@ -90,7 +104,10 @@ def test_large_logits_trigger_rescaling():
     q = (q.float() * 3).to(torch.bfloat16)
     for causal in (False, True):
         out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal)
-        assert _err(out, oracle.attention_fp32(q, k, v, causal)) <= ATOL
+        assert _err_scaled(out, oracle.attention_fp32(q, k, v, causal)) <= ATOL
+        q16, k16, v16 = (t.to(torch.float16) for t in (q, k, v))
+        out16 = llm_kernels.flash_attn_forward(q16.cuda(), k16.cuda(), v16.cuda(), causal=causal)
+        assert _err(out16, oracle.attention_fp32(q16, k16, v16, causal)) <= ATOL
 
 
 @pytest.mark.parametrize("causal", [True, False])
