@@ -7,21 +7,22 @@
 // Causal masking keeps key n for query m iff n <= m (top-left, :118) and skips key blocks
 // entirely above the diagonal (:112).
 //
-// CTA = one (batch, head) and 256 query rows held as two 128-row tiles (t = 0, 1) that
-// ping-pong on the tensor core.  10 warps:
+// CTA = one (batch, head) and 256 query rows held as two 128-row tiles (t = 0, 1).  10 warps:
 //   warps 0-3  softmax for tile 0 (thread = one query row = one TMEM lane)
 //   warps 4-7  softmax for tile 1
-//   warp  8    TMA producer: Q0/Q1 once, then K_0, V_0, K_1, V_1, ... through a ring of
-//              128-row stages (128B swizzle)
+//   warp  8    TMA producer: Q0/Q1 once, then K_0, K_1, V_0, K_2, V_1, ... (consumption
+//              order) through a ring of 128-row stages (128B swizzle)
 //   warp  9    TMEM owner + single-thread MMA issuer
-// Tensor memory (512 columns): S_t = cols [128t, 128t+128) fp32; P_t (bf16/f16 pairs) is
-// written over the first 64 columns of S_t; O_t = cols [256 + D*t, 256 + D*(t+1)) fp32.
-// MMA issue order per key block j:  S0(j), PV1(j-1), S1(j), PV0(j)  — so while softmax of
-// tile 0 runs on S0(j) the tensor core computes PV1(j-1) and S1(j), and vice versa.  Since
-// tcgen05 MMAs from one thread execute in order, the commit that publishes S_t(j) also
-// guarantees PV_t(j-1) finished: the softmax warps may rescale O_t right away.
+// Tensor memory (512 columns): S_t = cols [128t, 128t+128) fp32, O_t = cols
+// [256 + D*t, 256 + D*(t+1)) fp32.  P_t goes to shared memory (K-major, 128B swizzle) so the
+// PV product is a shared-memory x shared-memory MMA: on B200 an M128 N128 K16 MMA whose A
+// comes from TMEM costs ~115 cycles against ~77 with both operands in shared memory.
+// Since S_t no longer holds P, S for key block j+1 is issued as soon as the softmax of block
+// j has read S_t(j) into registers; per block j the MMA order is S0(j+1), S1(j+1), PV0(j),
+// PV1(j), which keeps the tensor core fed while the softmax of block j runs.
 // Rescaling is lazy: the running max used for exp2 only moves when the block max exceeds it
-// by more than 8 (log2 units), so P <= 256 and O is rarely touched.
+// by more than 8 (log2 units), so P <= 256 and O is rarely touched; the softmax warps do it
+// themselves once PV_t(j-1) has completed.
 // Every mbarrier wait is bounded; on failure all roles unwind and TMEM is freed.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -38,8 +39,14 @@ namespace fa {
 constexpr int kThreads = 320;
 constexpr int kTileM = 128;   // query rows per tile
 constexpr int kBlockN = 128;  // keys per block
-constexpr int kRingBytes = 128 * 1024;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+#ifndef LK_FA_POLY_PAIRS
+#define LK_FA_POLY_PAIRS 0
+#endif
+#ifndef LK_FA_GROUP_HEADS
+#define LK_FA_GROUP_HEADS 1  // 0: one global heavy-first order over all heads
+#endif
+constexpr int kPolyPairs = LK_FA_POLY_PAIRS;  // of every 16 exp2 pairs, this many on the FMA pipe
 
 enum Site : int {
   kSiteLoadQ = 201,
@@ -55,6 +62,7 @@ enum Site : int {
 struct Params {
   int B, H, M, N;
   int num_qblocks;  // ceil(M / 256)
+  int group_heads;  // heads per scheduling group (>= 1)
   int causal;
   float scale_log2;  // softmax scale * log2(e)
   void* o;
@@ -63,17 +71,79 @@ struct Params {
 
 template <int D>
 struct Cfg {
-  static constexpr int kQBoxes = D / 64;                 // 64-element (128 B) boxes per row
-  static constexpr int kTileBytes = kTileM * D * 2;      // one 128-row tile of Q, K or V
-  static constexpr int kStages = kRingBytes / kTileBytes;  // 4 (D=128) / 8 (D=64)
-  static constexpr int kSmemBytes = 2 * kTileBytes + kRingBytes + 1024 + 512;
+  static constexpr int kQBoxes = D / 64;               // 64-element (128 B) boxes per row
+  static constexpr int kTileBytes = kTileM * D * 2;    // one 128-row tile of Q, K or V
+  static constexpr int kPBytes = kTileM * kBlockN * 2; // one tile's P (32 KB)
+  static constexpr int kFixedBytes = 2 * kTileBytes + 2 * kPBytes;
+  static constexpr int kBudget = 232448 - 1024 - 512;  // opt-in smem - align slack - barriers
+  static constexpr int kStages = (kBudget - kFixedBytes) / kTileBytes;  // 3 (D=128) / 8 (D=64)
+  static constexpr int kSmemBytes = kFixedBytes + kStages * kTileBytes + 1024 + 512;
   static constexpr int kOCol0 = 256;
+  static_assert(kStages >= 3, "K/V ring needs three stages");
 };
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---- packed fp32x2 arithmetic (one instruction for two lanes of the FMA pipe) ------------
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void uf2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two lanes on the FMA/ALU pipes, relieving the MUFU pipe.  Cody-Waite split
+// x = r + f with r = round-to-nearest(x) (the 1.5*2^23 shifter leaves r in the low mantissa
+// bits) and f in [-0.5, 0.5]; 2^f from a cubic minimax polynomial fitted here by a Remez
+// exchange on relative error (max 7.5e-5 over [-0.5, 0.5]); 2^r added to the exponent
+// field.  x is clamped at -120 so the exponent never underflows.  Only used on key blocks
+// without masked (-inf) entries.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+  float x0, x1;
+  uf2(x, x0, x1);
+  x0 = fmaxf(x0, -120.f);
+  x1 = fmaxf(x1, -120.f);
+  const uint64_t xc = f2(x0, x1);
+  const uint64_t sh = f2(kShift, kShift);
+  const uint64_t t = add2(xc, sh);
+  const uint64_t f = sub2(xc, sub2(t, sh));
+  uint64_t p = fma2(f2(c3, c3), f, f2(c2, c2));
+  p = fma2(p, f, f2(c1, c1));
+  p = fma2(p, f, f2(c0, c0));
+  float t0, t1, p0, p1;
+  uf2(t, t0, t1);
+  uf2(p, p0, p1);
+  const float y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  const float y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return f2(y0, y1);
 }
 
 template <bool kBf16>
@@ -98,26 +168,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                          // [2][kTileBytes]
-  uint8_t* sRing = smem + 2 * C::kTileBytes;   // [S][kTileBytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kRingBytes);
+  uint8_t* sQ = smem;                                  // [2][kTileBytes]
+  uint8_t* sP = smem + 2 * C::kTileBytes;              // [2][kPBytes]
+  uint8_t* sRing = sP + 2 * C::kPBytes;                // [S][kTileBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + S * C::kTileBytes);
   uint64_t* q_full = bars;             // [1]
-  uint64_t* kv_full = bars + 1;        // [S]
-  uint64_t* kv_empty = kv_full + S;    // [S]
-  uint64_t* s_full = kv_empty + S;     // [2]
-  uint64_t* p_full = s_full + 2;       // [2]  128 arrivals each
-  uint64_t* o_full = p_full + 2;       // [2]
-  uint64_t* drain = o_full + 2;        // [1]
+  uint64_t* kv_full = bars + 1;        // [S]   TMA -> MMA
+  uint64_t* kv_empty = kv_full + S;    // [S]   MMA -> TMA (tcgen05.commit)
+  uint64_t* s_full = kv_empty + S;     // [2]   S_t(j) in TMEM (tcgen05.commit)
+  uint64_t* s_free = s_full + 2;       // [2]   softmax_t has S_t(j) in registers (4 warp arrivals)
+  uint64_t* p_full = s_free + 2;       // [2]   P_t(j) in smem, O_t rescaled (4 warp arrivals)
+  uint64_t* pv_done = p_full + 2;      // [2]   PV_t(j) finished: P_t smem free, O_t stable
+  uint64_t* exp_tok = pv_done + 2;     // [2]   exp_tok[t]: the other tile finished an exp phase
+  uint64_t* drain = exp_tok + 2;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
 
-  // Heavy-first ordering: the first B*H CTAs take the last (longest, when causal) q-block
-  // of every head.
+  // CTA order: heads are taken in groups of p.group_heads (about one wave of CTAs per group)
+  // so the CTAs resident at any time share a few heads' K/V in L2; inside a group the
+  // heaviest (last, when causal) q-blocks of every head go first.
   const int BH = p.B * p.H;
-  const int qb = p.num_qblocks - 1 - (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x % BH);
+  const int per_group = p.group_heads * p.num_qblocks;
+  const int grp = (int)(blockIdx.x / per_group);
+  const int gbase = grp * p.group_heads;
+  const int gsz = min(p.group_heads, BH - gbase);
+  const int rem = (int)(blockIdx.x - (unsigned)grp * per_group);
+  const int qb = p.num_qblocks - 1 - rem / gsz;
+  const int bh = gbase + rem % gsz;
   const int b = bh / p.H, h = bh % p.H;
   const int q0 = qb * 2 * kTileM;
   const int nkb = (p.N + kBlockN - 1) / kBlockN;
@@ -144,8 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], kTileM);
-      mbar_init(&o_full[t], 1);
+      mbar_init(&s_free[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&exp_tok[t], 4);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -182,8 +263,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&kv_full[slot], C::kTileBytes);
-        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
-        const int row = (i >> 1) * kBlockN;
+        // Ring order = MMA consumption order: K_0, then (K_{j+1}, V_j) for each j, S running
+        // one key block ahead of PV.
+        bool is_v;
+        int blk;
+        if (i == 0) {
+          is_v = false;
+          blk = 0;
+        } else if ((i & 1) && (i + 1) / 2 < J) {
+          is_v = false;
+          blk = (i + 1) / 2;
+        } else if (i & 1) {
+          is_v = true;
+          blk = J - 1;
+        } else {
+          is_v = true;
+          blk = (i - 2) / 2;
+        }
+        const CUtensorMap* tm = is_v ? &tmV : &tmK;
+        const int row = blk * kBlockN;
         uint8_t* dst = sRing + slot * C::kTileBytes;
         for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, h, b);
         issued = i + 1;
@@ -201,9 +299,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto item_addr = [&](int i) { return smem_u32(sRing + (i % S) * C::kTileBytes); };
       auto wait_item = [&](int i) { return mbar_wait(&kv_full[i % S], (i / S) & 1, kSiteMmaKV); };
       auto release_item = [&](int i) { tc_commit(&kv_empty[i % S]); };
-      // S_t = Q_t K_j^T : K-major A (Q) and B (K), K = D in steps of 16.
-      auto issue_s = [&](int t, int j) {
-        const uint32_t kb = item_addr(2 * j);
+      auto k_item = [&](int blk) { return blk == 0 ? 0 : 2 * blk - 1; };
+      auto v_item = [&](int blk) { return min(2 * blk + 2, 2 * J - 1); };
+      // S_t = Q_t K^T : K-major A (Q) and B (K), K = D in steps of 16.
+      auto issue_s = [&](int t, int blk) {
+        const uint32_t kb = item_addr(k_item(blk));
         const uint32_t d_tmem = tmem + t * kBlockN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
@@ -213,55 +313,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&s_full[t]);
       };
-      // O_t (+)= P_t V_j : A = P_t from TMEM (cols of S_t), B = V_j MN-major (D contiguous).
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t vb = item_addr(2 * j + 1);
+      // O_t (+)= P_t V : A = P_t from smem (K-major, 128B swizzle), B = V MN-major.
+      auto issue_pv = [&](int t, int blk) {
+        const uint32_t vb = item_addr(v_item(blk));
         const uint32_t o_tmem = tmem + C::kOCol0 + t * D;
-        const uint32_t p_tmem = tmem + t * kBlockN;
+        const uint32_t pb = smem_u32(sP + t * C::kPBytes);
 #pragma unroll
         for (int ks = 0; ks < kBlockN / 16; ++ks) {
-          mma_f16_ts(o_tmem, p_tmem + ks * 8, sdesc_sw128(vb + ks * 16 * 128, kTileM * 128, 1024), kIdescO,
-                     (j > 0 || ks > 0) ? 1u : 0u);
+          const uint32_t poff = (ks >> 2) * (kTileM * 128) + (ks & 3) * 32;
+          mma_f16_ss(o_tmem, sdesc_sw128(pb + poff, 16, 1024), sdesc_sw128(vb + ks * 16 * 128, kTileM * 128, 1024),
+                     kIdescO, (blk > 0 || ks > 0) ? 1u : 0u);
         }
-        if (j == nb[t] - 1) tc_commit(&o_full[t]);
+        tc_commit(&pv_done[t]);
       };
+      // Prologue: S_t(0) for both tiles.
+      if (ok && (ok = wait_item(0))) {
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t)
+          if (nb[t] > 0) issue_s(t, 0);
+        release_item(0);
+      }
       for (int j = 0; j < J && ok; ++j) {
-        if (!wait_item(2 * j)) {
+        // S for key block j+1 runs ahead of PV for block j: it only needs the softmax of
+        // block j to have read S_t(j) out of TMEM.
+        if (j + 1 < J) {
+          if (!wait_item(k_item(j + 1))) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j + 1 >= nb[t]) continue;
+            if (!mbar_wait(&s_free[t], j & 1, kSiteMmaP)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+          if (!ok) break;
+          release_item(k_item(j + 1));
+        }
+        if (!wait_item(v_item(j))) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        if (j < nb[0]) issue_s(0, j);
-        if (j >= 1 && j - 1 < nb[1]) {
-          if (!mbar_wait(&p_full[1], (j - 1) & 1, kSiteMmaP) || !wait_item(2 * j - 1)) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= nb[t]) continue;
+          if (!mbar_wait(&p_full[t], j & 1, kSiteMmaP)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(1, j - 1);
-          release_item(2 * j - 1);  // V_{j-1}: its last reader was PV1(j-1)
+          issue_pv(t, j);
         }
-        if (j < nb[1]) issue_s(1, j);
-        release_item(2 * j);  // K_j
-        if (j < nb[0]) {
-          if (!mbar_wait(&p_full[0], j & 1, kSiteMmaP) || !wait_item(2 * j + 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(0, j);
-          if (j >= nb[1]) release_item(2 * j + 1);  // tile 1 does not use V_j
-        } else if (j >= nb[1]) {
-          release_item(2 * j + 1);
-        }
-      }
-      if (ok && nb[1] > 0 && nb[1] == J) {
-        const int j = J - 1;
-        if (mbar_wait(&p_full[1], j & 1, kSiteMmaP) && wait_item(2 * j + 1)) {
-          tc_fence_after();
-          issue_pv(1, j);
-          release_item(2 * j + 1);
-        }
+        if (!ok) break;
+        release_item(v_item(j));
       }
       tc_commit(drain);
       mbar_wait(drain, 0, kSiteTeardown);
@@ -289,16 +395,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < kBlockN / 32; ++c) tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       tmem_wait_ld();
+      // S_t(j) is in registers: the MMA warp may overwrite S_t with block j+1 now.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[t]);
       const int n0 = j * kBlockN;
-      if (n0 + kBlockN - 1 > lim) {
+      // Tile-uniform: does any row of this tile see a masked key in block j?
+      const bool masked_block = (n0 + kBlockN > p.N) || (p.causal && n0 + kBlockN - 1 > q0 + t * kTileM);
+      if (masked_block && n0 + kBlockN - 1 > lim) {
 #pragma unroll
         for (int c = 0; c < kBlockN; ++c)
           if (n0 + c > lim) sr[c] = __float_as_uint(-INFINITY);
       }
       float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
 #pragma unroll
-      for (int c = 4; c < kBlockN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      for (int c = 4; c < kBlockN; c += 8) {
+        mx4[0] = max3(mx4[0], __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+        mx4[1] = max3(mx4[1], __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx4[2] = max3(mx4[2], __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx4[3] = max3(mx4[3], __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      const float mx = fmaxf(max3(mx4[0], mx4[1], mx4[2]), mx4[3]);
       const float m_new = mx * p.scale_log2;
       const bool need = m_new > m_used + kRescaleThreshold;
       const bool warp_rescale = __any_sync(0xffffffffu, need) && j > 0;
@@ -308,42 +425,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = m_new;
       }
       l *= alpha;
+      // The two tiles take turns on the exp phase (tile 0 block j, tile 1 block j, tile 0
+      // block j+1, ...): the MUFU pipe runs one tile's exponentials at full rate while the
+      // other tile loads S, reduces its max and stores P.  Tile 0 block j waits for tile 1's
+      // block j-1, tile 1 block j for tile 0's block j (skipped where the other tile has no
+      // such block); each tile's turns complete in order, so parities stay one phase apart.
+      if (t == 0 ? (j >= 1 && j - 1 < nb[1]) : (j < nb[0])) {
+        if (!mbar_wait(&exp_tok[t], (t == 0 ? j - 1 : j) & 1, kSiteSoftS)) {
+          ok = false;
+          break;
+        }
+      }
+      // p = 2^(s * scale * log2e - m_used), packed two per 32-bit word in the input dtype.
       const float neg = -m_used;
       float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pk[kBlockN / 2];
 #pragma unroll
-      for (int c = 0; c < kBlockN / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(__uint_as_float(sr[c * 32 + 2 * e]), p.scale_log2, neg));
-          const float p1 = ex2(fmaf(__uint_as_float(sr[c * 32 + 2 * e + 1]), p.scale_log2, neg));
-          rs0 += p0;
-          rs1 += p1;
-          pk[e] = pack2<kBf16>(p0, p1);
+      for (int e = 0; e < kBlockN / 2; ++e) {
+        float p0, p1;
+        if (e % 16 < kPolyPairs && !masked_block) {
+          uf2(exp2_poly2(f2(fmaf(__uint_as_float(sr[2 * e]), p.scale_log2, neg),
+                            fmaf(__uint_as_float(sr[2 * e + 1]), p.scale_log2, neg))),
+              p0, p1);
+        } else {
+          p0 = ex2(fmaf(__uint_as_float(sr[2 * e]), p.scale_log2, neg));
+          p1 = ex2(fmaf(__uint_as_float(sr[2 * e + 1]), p.scale_log2, neg));
         }
-        tmem_st16(s_tmem + c * 16, pk);
+        rs0 += p0;
+        rs1 += p1;
+        pk[e] = pack2<kBf16>(p0, p1);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&exp_tok[1 - t]);  // the other tile's turn
       l += rs0 + rs1;
-      if (warp_rescale) {
-        // O_t's last writer PV_t(j-1) completed before S_t(j) was published, and PV_t(j) is
-        // not issued before p_full below.  Done after P so the S registers are free.
+      if (j > 0) {
+        // PV_t(j-1) must be done before P_t is overwritten and O_t is rescaled.
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, kSiteSoftO)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (warp_rescale) {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(o_tmem + c * 32, ov);
-          tmem_wait_ld();
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(o_tmem + c * 32, ov);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st32(o_tmem + c * 32, ov);
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st32(o_tmem + c * 32, ov);
+          }
         }
       }
-      tmem_wait_st();
+      // P_t row r -> smem in the K-major 128B-swizzled layout the PV MMA reads: two 64-key
+      // halves of 128 rows x 128 B; 16-byte chunk c of row r lands at chunk c ^ (r & 7).
+      {
+        uint8_t* prow = sP + t * C::kPBytes + r * 128;
+#pragma unroll
+        for (int q = 0; q < kBlockN / 8; ++q) {
+          uint4 w = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(prow + (q >> 3) * (kTileM * 128) + ((((q & 7) ^ (r & 7))) << 4)) = w;
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy P stores -> visible to the tensor core
+      if (warp_rescale) tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // Epilogue: O / l -> global.
     if (ok && nb[t] > 0) {
-      if (mbar_wait(&o_full[t], 0, kSiteSoftO)) {
+      if (mbar_wait(&pv_done[t], (nb[t] - 1) & 1, kSiteSoftO)) {
         tc_fence_after();
         const float inv = 1.f / l;
         const bool row_ok = m < p.M;
@@ -436,6 +588,11 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   p.M = (int)M;
   p.N = (int)N;
   p.num_qblocks = (int)nqb;
+  {
+    // causal: two waves per group, so heavy-first ordering still balances the tail
+    const int64_t g = LK_FA_GROUP_HEADS ? (causal ? 2 : 1) * sm_count() / nqb : B * H;
+    p.group_heads = (int)(g < 1 ? 1 : (g > B * H ? B * H : g));
+  }
   p.causal = causal ? 1 : 0;
   const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = scale * 1.4426950408889634f;
