@@ -115,19 +115,62 @@ __device__ __forceinline__ int8_t quant_one(float x, float scale) {
   return (int8_t)(int)t;
 }
 
-__device__ __forceinline__ uint32_t pack4(int8_t a, int8_t b, int8_t c, int8_t d) {
-  return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
-         ((uint32_t)(uint8_t)d << 24);
+// The row's divisor, with its reciprocal for the fast path.
+struct RowScale {
+  float scale;
+  float rcp;
+  bool fast;  // scale is a positive normal finite number
+};
+
+__device__ __forceinline__ RowScale make_row_scale(float amax) {
+  RowScale s;
+  s.scale = __fdiv_rn(amax, 127.0f);
+  s.fast = (s.scale >= 1.17549435e-38f) && (s.scale < INFINITY);
+  s.rcp = s.fast ? __frcp_rn(s.scale) : 0.f;
+  return s;
+}
+
+// Same code as quant_one, usually without the division.  t = x * rcp differs from the
+// correctly rounded quotient fl(x / scale) by at most 2.3e-5 (|x / scale| <= 127.1: 2^-23
+// relative for the product and reciprocal, half an ulp of 127 for fl), so when t is more
+// than 2^-12 away from every half-integer both round to the same integer; only the rare
+// near-tie falls back to the IEEE division.
+// Rounding uses the 1.5 * 2^23 shifter: t + 1.5*2^23 rounds t to the nearest integer, ties
+// to even (exactly rintf), and leaves that integer in the low mantissa bits, so the int8
+// code is the low byte of the float's bits — no float->int conversion instruction needed.
+// The fast path only runs where |t| <= 127.1, so the code never needs clamping there.
+__device__ __forceinline__ int8_t quant_code(float x, const RowScale& s) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  if (s.fast) {
+    const float t = x * s.rcp;
+    const float tb = t + kShift;
+    if (fabsf(t - (tb - kShift)) <= 0.5f - 2.44140625e-4f) return (int8_t)(__float_as_uint(tb) & 0xFFu);
+  }
+  return quant_one(x, s.scale);
 }
 
 // Codes for one 16-byte vector, written to q (kElems bytes).
 template <typename T>
-__device__ __forceinline__ void quant_vec_store(const uint4& v, float scale, int8_t* q);
+__device__ __forceinline__ void quant_vec_store(const uint4& v, const RowScale& s, int8_t* q);
 template <>
-__device__ __forceinline__ void quant_vec_store<float>(const uint4& v, float scale, int8_t* q) {
-  uint32_t w = pack4(quant_one(__uint_as_float(v.x), scale), quant_one(__uint_as_float(v.y), scale),
-                     quant_one(__uint_as_float(v.z), scale), quant_one(__uint_as_float(v.w), scale));
-  *reinterpret_cast<uint32_t*>(q) = w;
+__device__ __forceinline__ void quant_vec_store<float>(const uint4& v, const RowScale& s, int8_t* q) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float f[4] = {__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)};
+  uint32_t b[4];
+  bool bad = !s.fast;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float t = f[e] * s.rcp;
+    const float tb = t + kShift;
+    bad |= !(fabsf(t - (tb - kShift)) <= 0.5f - 2.44140625e-4f);
+    b[e] = __float_as_uint(tb);
+  }
+  if (bad) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) b[e] = (uint32_t)(uint8_t)quant_one(f[e], s.scale);
+  }
+  *reinterpret_cast<uint32_t*>(q) =
+      __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
 }
 template <typename T16>
 __device__ __forceinline__ float lo16(uint32_t w);
@@ -150,20 +193,41 @@ __device__ __forceinline__ float hi16<__nv_bfloat16>(uint32_t w) {
   return __uint_as_float(w & 0xFFFF0000u);
 }
 template <typename T16>
-__device__ __forceinline__ void quant_vec16_store(const uint4& v, float scale, int8_t* q) {
-  uint32_t w0 = pack4(quant_one(lo16<T16>(v.x), scale), quant_one(hi16<T16>(v.x), scale),
-                      quant_one(lo16<T16>(v.y), scale), quant_one(hi16<T16>(v.y), scale));
-  uint32_t w1 = pack4(quant_one(lo16<T16>(v.z), scale), quant_one(hi16<T16>(v.z), scale),
-                      quant_one(lo16<T16>(v.w), scale), quant_one(hi16<T16>(v.w), scale));
+__device__ __forceinline__ void quant_vec16_store(const uint4& v, const RowScale& s, int8_t* q) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = lo16<T16>(w[j]);
+    f[2 * j + 1] = hi16<T16>(w[j]);
+  }
+  // Branch-free fast path for the whole vector (see quant_code); the exact division only
+  // runs for a vector holding a near-tie or in a row with a non-normal scale.
+  uint32_t b[8];
+  bool bad = !s.fast;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float t = f[e] * s.rcp;
+    const float tb = t + kShift;
+    bad |= !(fabsf(t - (tb - kShift)) <= 0.5f - 2.44140625e-4f);
+    b[e] = __float_as_uint(tb);
+  }
+  if (bad) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = (uint32_t)(uint8_t)quant_one(f[e], s.scale);
+  }
+  const uint32_t w0 = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
   *reinterpret_cast<uint2*>(q) = make_uint2(w0, w1);
 }
 template <>
-__device__ __forceinline__ void quant_vec_store<__half>(const uint4& v, float scale, int8_t* q) {
-  quant_vec16_store<__half>(v, scale, q);
+__device__ __forceinline__ void quant_vec_store<__half>(const uint4& v, const RowScale& s, int8_t* q) {
+  quant_vec16_store<__half>(v, s, q);
 }
 template <>
-__device__ __forceinline__ void quant_vec_store<__nv_bfloat16>(const uint4& v, float scale, int8_t* q) {
-  quant_vec16_store<__nv_bfloat16>(v, scale, q);
+__device__ __forceinline__ void quant_vec_store<__nv_bfloat16>(const uint4& v, const RowScale& s, int8_t* q) {
+  quant_vec16_store<__nv_bfloat16>(v, s, q);
 }
 
 __device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
@@ -207,14 +271,52 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     }
   }
   m = warp_max_u32(m);
-  const float amax = bits_to_float<T>(m);
-  const float scale = __fdiv_rn(amax, 127.0f);
-  if (lane == 0) scale_out[row] = scale;
+  const RowScale s = make_row_scale(bits_to_float<T>(m));
+  if (lane == 0) scale_out[row] = s.scale;
   int8_t* qr = q + row * q_ld;
 #pragma unroll
   for (int i = 0; i < kVecs; ++i) {
     const int64_t vi = (int64_t)i * 32 + lane;
-    if (vi < nvec) quant_vec_store<T>(cache[i], scale, qr + vi * E);
+    if (vi < nvec) quant_vec_store<T>(cache[i], s, qr + vi * E);
+  }
+}
+
+// Vector path for wide rows: one CTA of kRowThreads threads per row, each caching up to
+// kVecs 16-byte vectors; the absmax is reduced across warps through shared memory.  Many
+// rows stay in flight per SM, which is what an HBM-bound pass needs.
+template <typename T, int kRowThreads, int kVecs>
+__global__ void __launch_bounds__(kRowThreads)
+    quantize_rows_cta(const T* __restrict__ x, int64_t cols, int64_t x_ld, int8_t* __restrict__ q, int64_t q_ld,
+                      float* __restrict__ scale_out) {
+  constexpr int E = VecTraits<T>::kElems;
+  constexpr int kWarps = kRowThreads / 32;
+  __shared__ uint32_t warp_max[kWarps];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * x_ld);
+  const int64_t nvec = cols / E;
+  uint4 cache[kVecs];
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < kVecs; ++i) {
+    const int64_t vi = (int64_t)i * kRowThreads + tid;
+    if (vi < nvec) {
+      cache[i] = ld_stream(xv + vi);
+      m = max(m, vec_absmax_bits<T>(cache[i]));
+    }
+  }
+  m = warp_max_u32(m);
+  if ((tid & 31) == 0) warp_max[tid >> 5] = m;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) m = max(m, warp_max[w]);
+  const RowScale s = make_row_scale(bits_to_float<T>(m));
+  if (tid == 0) scale_out[row] = s.scale;
+  int8_t* qr = q + row * q_ld;
+#pragma unroll
+  for (int i = 0; i < kVecs; ++i) {
+    const int64_t vi = (int64_t)i * kRowThreads + tid;
+    if (vi < nvec) quant_vec_store<T>(cache[i], s, qr + vi * E);
   }
 }
 
@@ -230,10 +332,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   uint32_t m = 0;
   for (int64_t c = lane; c < cols; c += 32) m = max(m, mag_bits<T>(xr[c]));
   m = warp_max_u32(m);
-  const float scale = __fdiv_rn(bits_to_float<T>(m), 127.0f);
-  if (lane == 0) scale_out[row] = scale;
+  const RowScale s = make_row_scale(bits_to_float<T>(m));
+  if (lane == 0) scale_out[row] = s.scale;
   int8_t* qr = q + row * q_ld;
-  for (int64_t c = lane; c < cols; c += 32) qr[c] = quant_one(to_f32<T>(xr[c]), scale);
+  for (int64_t c = lane; c < cols; c += 32) qr[c] = quant_code(to_f32<T>(xr[c]), s);
 }
 
 template <typename T>
@@ -246,14 +348,17 @@ int launch_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_ld, int
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((x_ld * (int64_t)sizeof(T)) % 16 == 0) &&
                        (cols % E == 0) && ((reinterpret_cast<uintptr_t>(q) & 7) == 0) && (q_ld % 8 == 0);
   const int64_t nvec = cols / E;
+  const bool cta_rows = rows <= 0x7FFFFFFF;
   if (aligned && nvec <= 32 * 4) {
     quantize_rows_cached<T, 4><<<grid, block, 0, stream>>>(xt, rows, cols, x_ld, q, q_ld, scale);
-  } else if (aligned && nvec <= 32 * 8) {
-    quantize_rows_cached<T, 8><<<grid, block, 0, stream>>>(xt, rows, cols, x_ld, q, q_ld, scale);
-  } else if (aligned && nvec <= 32 * 16) {
-    quantize_rows_cached<T, 16><<<grid, block, 0, stream>>>(xt, rows, cols, x_ld, q, q_ld, scale);
-  } else if (aligned && nvec <= 32 * 32) {
-    quantize_rows_cached<T, 32><<<grid, block, 0, stream>>>(xt, rows, cols, x_ld, q, q_ld, scale);
+  } else if (aligned && cta_rows && nvec <= 128 * 4) {
+    quantize_rows_cta<T, 128, 4><<<(unsigned)rows, 128, 0, stream>>>(xt, cols, x_ld, q, q_ld, scale);
+  } else if (aligned && cta_rows && nvec <= 256 * 4) {
+    quantize_rows_cta<T, 256, 4><<<(unsigned)rows, 256, 0, stream>>>(xt, cols, x_ld, q, q_ld, scale);
+  } else if (aligned && cta_rows && nvec <= 512 * 4) {
+    quantize_rows_cta<T, 512, 4><<<(unsigned)rows, 512, 0, stream>>>(xt, cols, x_ld, q, q_ld, scale);
+  } else if (aligned && cta_rows && nvec <= 512 * 8) {
+    quantize_rows_cta<T, 512, 8><<<(unsigned)rows, 512, 0, stream>>>(xt, cols, x_ld, q, q_ld, scale);
   } else {
     quantize_rows_generic<T><<<grid, block, 0, stream>>>(xt, rows, cols, x_ld, q, q_ld, scale);
   }

@@ -59,6 +59,24 @@ def test_quantize_special_rows():
         _check(x.to(dt).cuda())
 
 
+def test_quantize_near_ties_take_the_exact_path():
+    """Rows built so that many x / scale land exactly on, or within an ulp of, k + 0.5: the
+    reciprocal fast path must hand those to the IEEE division and still match bit for bit."""
+    rows = []
+    g = torch.Generator().manual_seed(17)
+    for a in (1.0, 0.37, 3.0e-3, 1.7e4, 1.1754944e-38 * 512):
+        base = torch.arange(-127, 127, dtype=torch.float64) + 0.5
+        jitter = torch.tensor([-1, 0, 1], dtype=torch.float64)
+        vals = (base[:, None] * (1 + jitter[None, :] * 2.0 ** -23)).flatten()
+        row = torch.cat([torch.tensor([127.0], dtype=torch.float64), vals])[:768] * a
+        rows.append(row.float())
+    x = torch.stack(rows)
+    x = x[:, torch.randperm(x.shape[1], generator=g)]
+    for dt in (torch.float32, torch.float16, torch.bfloat16):
+        _check(x.to(dt).cuda())
+        _check(x.to(dt).repeat(1, 8).cuda())  # wide-row (CTA-per-row) kernels
+
+
 def test_quantize_strided_rows_and_leading_dims():
     base = torch.randn(16, 300, dtype=torch.float16).cuda()
     _check(base[:, :256])  # row stride 300 != cols
