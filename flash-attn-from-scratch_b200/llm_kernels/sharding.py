@@ -1,0 +1,96 @@
+"""Multi-GPU partitioning of the op set (one process per GPU, torch.distributed).
+
+Every op shards without communication on its data path:
+  * attention over batch x heads, quantisation over rows, the GEMMs over tokens (rows of A /
+    x) with replicated weights -> ``shard_range`` / ``shard_rows``;
+  * optionally a weight is split by output columns (N / g per rank) and the ``[M, N/g]``
+    partial outputs are gathered into a replicated ``[M, N]`` with one
+    ``all_gather_into_tensor`` -> ``shard_columns`` / ``gather_columns`` /
+    ``column_sharded_int8_linear``.
+The gather is the only collective; it runs over NCCL on GPUs and over gloo in the CPU tests.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+__all__ = [
+    "shard_range",
+    "shard_rows",
+    "gather_rows",
+    "shard_columns",
+    "gather_columns",
+    "column_sharded_int8_linear",
+]
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous [start, stop) of ``n`` items for ``rank`` of ``world``; sizes differ by <= 1."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    if n < 0:
+        raise ValueError("n must be >= 0")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard_rows(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
+    """This rank's slice of ``t`` along ``dim`` (a view, no copy)."""
+    s, e = shard_range(t.shape[dim], rank, world)
+    return t.narrow(dim, s, e - s)
+
+
+def _world(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def gather_rows(local: torch.Tensor, total_rows: int, group=None) -> torch.Tensor:
+    """Inverse of ``shard_rows`` along dim 0: every rank receives the full tensor.  Uneven
+    shards are padded to the largest shard for the collective and trimmed afterwards."""
+    world, _ = _world(group)
+    cap = -(-total_rows // world)
+    pad = torch.zeros((cap,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]].copy_(local)
+    out = torch.empty((world * cap,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, pad, group=group)
+    pieces = []
+    for r in range(world):
+        s, e = shard_range(total_rows, r, world)
+        pieces.append(out[r * cap: r * cap + (e - s)])
+    return torch.cat(pieces, 0)
+
+
+def shard_columns(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Output-column shard of a weight stored ``[N, K]`` (its rows), contiguous."""
+    return shard_rows(w, rank, world, 0).contiguous()
+
+
+def gather_columns(local: torch.Tensor, n_total: int, group=None) -> torch.Tensor:
+    """``[M, N_r]`` per rank -> replicated ``[M, n_total]`` with rank r's columns at its
+    ``shard_range``.  One ``all_gather_into_tensor`` of equal-sized (padded) blocks."""
+    world, _ = _world(group)
+    M = local.shape[0]
+    cap = -(-n_total // world)
+    blk = torch.zeros((M, cap), dtype=local.dtype, device=local.device)
+    blk[:, : local.shape[1]].copy_(local)
+    out = torch.empty((world, M, cap), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out.view(world * M, cap), blk, group=group)
+    cols = []
+    for r in range(world):
+        s, e = shard_range(n_total, r, world)
+        cols.append(out[r, :, : e - s])
+    return torch.cat(cols, 1)
+
+
+def column_sharded_int8_linear(x: torch.Tensor, w_q_shard: torch.Tensor, scale_w_shard: torch.Tensor,
+                               n_total: int, group=None, replicate: bool = True) -> torch.Tensor:
+    """Tensor-parallel ``Int8Linear`` forward: quantise ``x`` (replicated), multiply by this
+    rank's ``[N/g, K]`` weight shard with the sm_100a int8 GEMM, then (``replicate=True``)
+    gather the ``[M, N/g]`` fp16 blocks into ``[M, N]`` on every rank."""
+    from .int8_gemm import int8_gemm_dequant_nk, quantize_symmetric
+
+    xq, sx = quantize_symmetric(x)
+    y = int8_gemm_dequant_nk(xq, w_q_shard, sx, scale_w_shard)
+    return gather_columns(y, n_total, group) if replicate else y
