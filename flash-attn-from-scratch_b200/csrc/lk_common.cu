@@ -110,6 +110,8 @@ const char* lk_status_string(int status) {
       return "device pipeline wait timed out";
     case LK_ERR_ALIGNMENT:
       return "pointer or stride not 16-byte aligned";
+    case LK_ERR_SCRATCH_LIMIT:
+      return "problem exceeds the fixed scratch of a no-allocation entry point (rows > 65536)";
     default:
       return "unknown status";
   }

@@ -18,6 +18,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "gemm_sm100.cuh"
 #include "lk_abi.h"
 
@@ -251,4 +253,49 @@ extern "C" int lk_fused_rmsnorm_linear(const void* X, const void* W_norm, const 
                                        float* row_rstd, void* stream) {
   if (int st = lk_rmsnorm_linear_fold(W_norm, dtype, W_lin, w_fold, dtype, D_in, D_out, stream)) return st;
   return lk_rmsnorm_linear(X, D_in, w_fold, Y, D_out, dtype, B, D_in, D_out, eps, row_rstd, stream);
+}
+
+// ---- RMSNorm + Linear without any caller-provided scratch -----------------------------------
+// For callers that cannot allocate device memory at the point of the call (see the header):
+// the per-row rsqrt scratch that lk_rmsnorm_linear takes as `row_rstd` lives in this file-scope
+// array instead.  Host code must not pass `g_static_rstd` itself to a kernel — on the host that
+// name is only a stand-in — so its device address is looked up once per device, with that
+// device current, and cached.
+namespace lk {
+namespace {
+constexpr int64_t kStaticRstdRows = 65536;  // 256 KiB of fp32 on every device that loads the library
+static __device__ __align__(256) float g_static_rstd[kStaticRstdRows];
+constexpr int kStaticDevices = 64;
+std::mutex g_static_mu;
+float* g_static_rstd_addr[kStaticDevices];
+
+int static_rstd_address(float** out) {
+  int dev = -1;
+  if (int st = cuda_status(cudaGetDevice(&dev))) return st;
+  if (dev < 0 || dev >= kStaticDevices) return LK_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_rstd_addr[dev]) {
+    void* p = nullptr;
+    if (int st = cuda_status(cudaGetSymbolAddress(&p, g_static_rstd))) return st;
+    g_static_rstd_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_static_rstd_addr[dev];
+  return LK_OK;
+}
+}  // namespace
+}  // namespace lk
+
+extern "C" int lk_rmsnorm_linear_noalloc(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld,
+                                         int dtype, int64_t rows, int64_t d_in, int64_t d_out, float eps,
+                                         void* stream) {
+  using namespace lk;
+  if (rows < 0 || d_in < 0 || d_out < 0) return LK_ERR_INVALID_ARG;
+  if (rows > kStaticRstdRows) return LK_ERR_SCRATCH_LIMIT;
+  if (rows == 0 || d_out == 0) return LK_OK;
+  if (int st = bind_stream(static_cast<cudaStream_t>(stream))) return st;
+  float* rstd = nullptr;
+  if (int st = static_rstd_address(&rstd)) return st;
+  // Every element of rstd[0, rows) is written by the row kernel before the GEMM reads it, so
+  // whatever the previous call left in the array needs no clearing.
+  return lk_rmsnorm_linear(x, x_ld, w_fold, y, y_ld, dtype, rows, d_in, d_out, eps, rstd, stream);
 }

@@ -21,6 +21,7 @@ LK_ERR_UNSUPPORTED = 2
 LK_ERR_CUDA = 3
 LK_ERR_TIMEOUT = 4
 LK_ERR_ALIGNMENT = 5
+LK_ERR_SCRATCH_LIMIT = 6
 
 LK_F32, LK_F16, LK_BF16, LK_I8, LK_I32 = 0, 1, 2, 3, 4
 
@@ -48,6 +49,7 @@ SIGNATURES = {
     "lk_rmsnorm_linear_fold": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _p]),
     "lk_rmsnorm_linear": (_i, [_p, _i64, _p, _p, _i64, _i, _i64, _i64, _i64, _f, _p, _p]),
     "lk_fused_rmsnorm_linear": (_i, [_p, _p, _p, _p, _f, _i64, _i64, _i64, _i, _p, _p, _p]),
+    "lk_rmsnorm_linear_noalloc": (_i, [_p, _i64, _p, _p, _i64, _i, _i64, _i64, _i64, _f, _p]),
 }
 
 _lib = None

@@ -37,7 +37,8 @@ typedef enum {
   LK_ERR_UNSUPPORTED = 2,   /* dtype / head dim / layout this build does not implement           */
   LK_ERR_CUDA = 3,          /* a CUDA runtime or driver call failed (see lk_last_cuda_error)    */
   LK_ERR_TIMEOUT = 4,       /* a device-side pipeline wait ran out (from lk_device_status)      */
-  LK_ERR_ALIGNMENT = 5      /* pointer or stride not 16-byte aligned where TMA needs it          */
+  LK_ERR_ALIGNMENT = 5,     /* pointer or stride not 16-byte aligned where TMA needs it          */
+  LK_ERR_SCRATCH_LIMIT = 6  /* problem larger than a no-allocation entry point's fixed scratch   */
 } lk_status;
 
 /* ---- dtype codes ------------------------------------------------------------------------- */
@@ -140,6 +141,25 @@ LK_API int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, vo
 LK_API int lk_fused_rmsnorm_linear(const void* X, const void* W_norm, const void* W_lin, void* Y,
                                    float eps, int64_t B, int64_t D_in, int64_t D_out, int dtype,
                                    void* w_fold, float* row_rstd, void* stream);
+
+/* lk_rmsnorm_linear without the row_rstd scratch argument.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory when they call the op: an engine that
+ * plans every device buffer ahead of time and hands kernels only those buffers, or a
+ * plugin host that gives its plugins no allocator.  Such callers still provide x, w_fold
+ * (from lk_rmsnorm_linear_fold) and y; the per-row rsqrt scratch lives in a fixed array
+ * inside this library, 65536 fp32 values (256 KiB) that every GPU loading the library holds
+ * until the process exits.  rows > 65536 returns LK_ERR_SCRATCH_LIMIT before any launch.
+ * The entry point itself calls no allocating function.
+ *
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress)
+ * and caches it; make that first call before any stream capture begins.  All calls on a
+ * device share the one array, so calls that can overlap on the GPU (different streams
+ * without ordering between them) race on it; calls on one stream are ordered and safe.
+ * Nothing in the array needs to start at zero: each call overwrites every value it reads. */
+LK_API int lk_rmsnorm_linear_noalloc(const void* x, int64_t x_ld, const void* w_fold, void* y,
+                                     int64_t y_ld, int dtype, int64_t rows, int64_t d_in,
+                                     int64_t d_out, float eps, void* stream);
 
 #ifdef __cplusplus
 }
