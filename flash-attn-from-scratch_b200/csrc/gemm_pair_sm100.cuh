@@ -1,0 +1,292 @@
+// gemm_pair_sm100.cuh — the GEMM of gemm_sm100.cuh on a CTA pair (cluster of 2, tcgen05
+// cta_group::2): output tiles of 256 x 256 per pair, 128 rows per CTA.
+//
+// Why: with one CTA per 128 x 256 tile every SM streams 16 KB of A and 32 KB of B per 128-byte
+// K slice; on a pair each CTA streams only its own 16 KB of A and its 16 KB half of B, and the
+// even CTA's single MMA instruction (M=256, N=256) multiplies both halves.  Operand traffic
+// per SM (L2 -> SMEM and SMEM -> tensor core) drops by a third for the same work.
+//
+// Roles per CTA (6 warps, as in the one-CTA kernel):
+//   warp 0     TMA producer in BOTH CTAs: each loads its own A rows and its half of B into its
+//              own shared memory; completion bytes of both are counted on the EVEN CTA's
+//              barrier, on which only the even CTA's producer arrives (announcing both CTAs'
+//              bytes) — a remote release-arrive from the peer was measured to serialise the
+//              ring (~1200 cycles per slot).
+//   warp 1     TMEM owner in both CTAs (pair allocation); MMA issuer in the even CTA only:
+//              tcgen05.mma.cta_group::2, then one commit to each CTA's ring-slot barrier and,
+//              per tile, to each CTA's accumulator barrier (no multicast qualifier: the peer's
+//              barrier is addressed through mapa).
+//   warps 2-5  epilogue in both CTAs: each drains its own 128 rows x 256 columns from its TMEM
+//              and tells the even CTA (local or remote arrive) when the buffer is free.
+// The pair synchronises with barrier.cluster after set-up and before TMEM is released, so no
+// CTA exits while its peer may still read its shared memory.  All mbarrier waits are bounded.
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace lk {
+namespace gemm {
+
+template <Kind kKind, bool kBMN>
+struct PairConfig {
+  using KT = KindTraits<kKind>;
+  static constexpr int kBN = 256;     // pair tile N
+  static constexpr int kHalfN = 128;  // B columns held by each CTA
+  static constexpr int kBK = kBKBytes / KT::kElemBytes;
+  static constexpr int kMmasPerStage = kBK / KT::kMmaK;
+  static constexpr int kABytes = kBM * kBKBytes;     // 16 KB
+  static constexpr int kBBytes = kHalfN * kBKBytes;  // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 6;
+  static constexpr int kBBoxes = kBMN ? (kHalfN * KT::kElemBytes) / 128 : 1;
+  static constexpr int kBBoxBytes = kBMN ? kBK * 128 : kBBytes;
+  static constexpr int kTmemCols = 2 * kBN;  // double-buffered 256-column accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr uint32_t kIdesc =
+      make_idesc(KT::kCFmt, KT::kAFmt, KT::kBFmt, 0u, kBMN ? 1u : 0u, 2u * kBM, (uint32_t)kBN);
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+enum PairSite : int {
+  kSitePairEmpty = 121,
+  kSitePairAccEmpty = 122,
+  kSitePairFull = 123,
+  kSitePairAccFull = 124,
+  kSitePairTeardown = 125,
+};
+
+template <Kind kKind, bool kBMN, Epi kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const Params p) {
+  using Cfg = PairConfig<kKind, kBMN>;
+  using KT = typename Cfg::KT;
+  constexpr int S = Cfg::kStages;
+  constexpr int kPairM = 2 * kBM;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;               // [S]  (even CTA's copy used) both CTAs' TMA bytes -> MMA
+  uint64_t* empty = bars + S;          // [S]  MMA commit -> each CTA's producer
+  uint64_t* acc_full = bars + 2 * S;   // [2]  MMA commit -> each CTA's epilogue
+  uint64_t* acc_empty = acc_full + 2;  // [2]  (even CTA's copy used) 8 epilogue warps -> MMA
+  uint64_t* drain = acc_empty + 2;     // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = (int)(blockIdx.x >> 1);
+  const int npairs = (int)(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (p.K + Cfg::kBK - 1) / Cfg::kBK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+        int mb, nb;
+        tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+        const int m0 = mb * kPairM + (int)rank * kBM;
+        const int n0 = nb * Cfg::kBN + (int)rank * Cfg::kHalfN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, kSitePairEmpty) || *(volatile int*)abort_flag) {
+            ok = false;
+            break;
+          }
+          // Only the even CTA arrives, announcing both CTAs' bytes; the peer's copies just
+          // complete their bytes on that barrier (its transaction count may dip below zero
+          // until the announcement lands, which mbarriers allow).  A remote release-arrive
+          // from the peer would wait for its earlier copies and serialise the ring.
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          const uint32_t lbar = pair_leader_addr(&full[stage]);
+          const int kx = kb * kBKBytes / KT::kElemBytes;
+          tma_load_2d_pair(sA + stage * Cfg::kABytes, &tmA, lbar, kx, m0);
+          uint8_t* dstB = sB + stage * Cfg::kBBytes;
+          if constexpr (kBMN) {
+#pragma unroll
+            for (int b = 0; b < Cfg::kBBoxes; ++b)
+              tma_load_2d_pair(dstB + b * Cfg::kBBoxBytes, &tmB, lbar, n0 + b * (128 / KT::kElemBytes), kx);
+          } else {
+            tma_load_2d_pair(dstB, &tmB, lbar, kx, n0);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) *(volatile int*)abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int t = pair; t < p.num_tiles && ok; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kBN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(&full[stage], phase, kSitePairFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int ks = 0; ks < Cfg::kMmasPerStage; ++ks) {
+            const uint64_t adesc = sdesc_sw128(a_base + ks * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (kBMN)
+              bdesc = sdesc_sw128(b_base + ks * KT::kMmaK * 128, Cfg::kBBoxBytes, 1024);
+            else
+              bdesc = sdesc_sw128(b_base + ks * 32, 16, 1024);
+            if constexpr (kKind == Kind::I8)
+              mma_i8_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb | ks) != 0);
+            else
+              mma_f16_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb | ks) != 0);
+          }
+          tc_commit_pair(cluster_addr(&empty[stage], 0));
+          tc_commit_pair(cluster_addr(&empty[stage], 1));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(cluster_addr(&acc_full[acc], 0));
+        tc_commit_pair(cluster_addr(&acc_full[acc], 1));
+      }
+      if (!ok) *(volatile int*)abort_flag = 1;
+      tc_commit_pair(cluster_addr(drain, 0));
+      mbar_wait(drain, 0, kSitePairTeardown);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both)
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+      int mb, nb;
+      tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+      const int m = mb * kPairM + (int)rank * kBM + row_in_tile;
+      const int n_base = nb * Cfg::kBN;
+      const bool row_ok = m < p.M;
+      float row_scale = 0.f;
+      if constexpr (kEpi == Epi::DequantF16) {
+        row_scale = row_ok ? __ldg(p.sa + m) : 0.f;
+      } else if constexpr (kEpi == Epi::RowRsqrt) {
+        if (local == 0) griddep_wait();
+        row_scale = row_ok ? __ldcg(p.rstd + m) : 0.f;
+      }
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSitePairAccFull)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * Cfg::kBN);
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_wait_ld();
+        if (c == Cfg::kBN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader)
+              mbar_arrive(&acc_empty[acc]);
+            else
+              mbar_arrive_remote(&acc_empty[acc], 0);
+          }
+        }
+        const int n0 = n_base + c * 32;
+        if (!row_ok || n0 >= p.N) continue;
+        store_chunk<kKind, kEpi>(r, row_scale, m, n0, p);
+      }
+      if (*(volatile int*)abort_flag) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the even CTA's MMAs are drained: no peer smem is read after this
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+}
+
+template <Kind kKind, bool kBMN, Epi kEpi>
+int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Params& p, int num_sms, cudaStream_t stream) {
+  using Cfg = PairConfig<kKind, kBMN>;
+  auto kern = gemm_pair_kernel<kKind, kBMN, kEpi>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return (int)e;
+    configured.fetch_or(bit);
+  }
+  const int pairs = p.num_tiles < num_sms / 2 ? p.num_tiles : num_sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = (kEpi == Epi::RowRsqrt) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+}
+
+}  // namespace gemm
+}  // namespace lk

@@ -127,6 +127,74 @@ __device__ __forceinline__ uint32_t pack_bf162(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Stores one 32-column chunk of accumulator row m (columns n0..n0+31) with the op's epilogue.
+template <Kind kKind, Epi kEpi>
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_scale, int m, int n0, const Params& p) {
+  const bool full_chunk = (n0 + 32 <= p.N);
+  if constexpr (kEpi == Epi::RawI32) {
+    int32_t* crow = static_cast<int32_t*>(p.C) + (int64_t)m * p.ldc + n0;
+    if (full_chunk && (p.ldc % 4 == 0)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<uint4*>(crow)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) crow[j] = (int32_t)r[j];
+    }
+  } else {
+    float v[32];
+    if constexpr (kEpi == Epi::DequantF16) {
+      // Bit-exact order of the reference epilogue: (fp32(acc) * sa[m]) * sb[n].
+      const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0);
+      if (full_chunk && ((reinterpret_cast<uintptr_t>(p.sb + n0) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 s4 = __ldg(sb4 + j);
+          v[4 * j + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 0]), row_scale), s4.x);
+          v[4 * j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 1]), row_scale), s4.y);
+          v[4 * j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 2]), row_scale), s4.z);
+          v[4 * j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 3]), row_scale), s4.w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sbj = (n0 + j < p.N) ? __ldg(p.sb + n0 + j) : 0.f;
+          v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), row_scale), sbj);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
+    }
+    uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
+    constexpr bool kBf16Out = (kEpi == Epi::RowRsqrt && kKind == Kind::BF16);
+    if (full_chunk && (p.ldc % 8 == 0)) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 w;
+        if constexpr (kBf16Out) {
+          w = make_uint4(pack_bf162(v[8 * j], v[8 * j + 1]), pack_bf162(v[8 * j + 2], v[8 * j + 3]),
+                         pack_bf162(v[8 * j + 4], v[8 * j + 5]), pack_bf162(v[8 * j + 6], v[8 * j + 7]));
+        } else {
+          w = make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                         pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+        }
+        reinterpret_cast<uint4*>(crow)[j] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (n0 + j >= p.N) continue;
+        if constexpr (kBf16Out)
+          crow[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+        else
+          crow[j] = __half_as_ushort(__float2half_rn(v[j]));
+      }
+    }
+  }
+}
+
 // ---- the kernel ---------------------------------------------------------------------------
 template <Kind kKind, int BN, bool kBMN, Epi kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -321,69 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int n0 = n_base + c * 32;
         if (!row_ok || n0 >= p.N) continue;
-        const bool full_chunk = (n0 + 32 <= p.N);
-        if constexpr (kEpi == Epi::RawI32) {
-          int32_t* crow = static_cast<int32_t*>(p.C) + (int64_t)m * p.ldc + n0;
-          if (full_chunk && (p.ldc % 4 == 0)) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              reinterpret_cast<uint4*>(crow)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) crow[j] = (int32_t)r[j];
-          }
-        } else {
-          float v[32];
-          if constexpr (kEpi == Epi::DequantF16) {
-            // Bit-exact order of the reference epilogue: (fp32(acc) * sa[m]) * sb[n].
-            const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0);
-            if (full_chunk && ((reinterpret_cast<uintptr_t>(p.sb + n0) & 15) == 0)) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 s4 = __ldg(sb4 + j);
-                v[4 * j + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 0]), row_scale), s4.x);
-                v[4 * j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 1]), row_scale), s4.y);
-                v[4 * j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 2]), row_scale), s4.z);
-                v[4 * j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 3]), row_scale), s4.w);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float sbj = (n0 + j < p.N) ? __ldg(p.sb + n0 + j) : 0.f;
-                v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), row_scale), sbj);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
-          }
-          uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
-          constexpr bool kBf16Out = (kEpi == Epi::RowRsqrt && kKind == Kind::BF16);
-          if (full_chunk && (p.ldc % 8 == 0)) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 w;
-              if constexpr (kBf16Out) {
-                w = make_uint4(pack_bf162(v[8 * j], v[8 * j + 1]), pack_bf162(v[8 * j + 2], v[8 * j + 3]),
-                               pack_bf162(v[8 * j + 4], v[8 * j + 5]), pack_bf162(v[8 * j + 6], v[8 * j + 7]));
-              } else {
-                w = make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
-                               pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
-              }
-              reinterpret_cast<uint4*>(crow)[j] = w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (n0 + j >= p.N) continue;
-              if constexpr (kBf16Out)
-                crow[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
-              else
-                crow[j] = __half_as_ushort(__float2half_rn(v[j]));
-            }
-          }
-        }
+        store_chunk<kKind, kEpi>(r, row_scale, m, n0, p);
       }
       if (*(volatile int*)abort_flag) break;
     }

@@ -5,7 +5,7 @@
 //   C[m,n]   = fp16(fp32(acc) * sa[m] * sb[n])  evaluated left to right (:84), RN conversion
 // on sm_100a: the int32 accumulator lives in tensor memory and is dequantised straight from
 // TMEM in the epilogue, so it never touches HBM.
-#include "gemm_sm100.cuh"
+#include "gemm_pair_sm100.cuh"
 #include "lk_abi.h"
 
 namespace lk {
@@ -55,6 +55,32 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   if (int st = bind_stream(stream)) return st;
 
   const int num_sms = sm_count();
+#ifndef LK_GEMM_PAIR
+#define LK_GEMM_PAIR 1
+#endif
+  {
+    // CTA pairs with 256 x 256 tiles when there are enough of them to occupy every pair.
+    const int ptm = (int)((M + 255) / 256), ptn = (int)((N + 255) / 256);
+    if (LK_GEMM_PAIR && (int64_t)ptm * ptn >= num_sms / 2) {
+      CUtensorMap ta, tb;
+      if (int st = make_int8_maps(A, lda, B, ldb, b_mn, (int)M, (int)N, (int)K, 128, &ta, &tb)) return st;
+      gemm::Params p{};
+      p.M = (int)M;
+      p.N = (int)N;
+      p.K = (int)K;
+      p.tiles_m = ptm;
+      p.tiles_n = ptn;
+      p.num_tiles = ptm * ptn;
+      p.C = C;
+      p.ldc = ldc;
+      p.sa = sa;
+      p.sb = sb;
+      p.rstd = nullptr;
+      const int err = b_mn ? gemm::launch_pair<Kind::I8, true, kEpi>(ta, tb, p, num_sms, stream)
+                           : gemm::launch_pair<Kind::I8, false, kEpi>(ta, tb, p, num_sms, stream);
+      return cuda_status((cudaError_t)err);
+    }
+  }
   const int tiles_m = (int)((M + gemm::kBM - 1) / gemm::kBM);
   // Wide tiles halve operand traffic per MMA; narrow ones only when wide ones cannot fill the GPU.
   const int tiles_n256 = (int)((N + 255) / 256);

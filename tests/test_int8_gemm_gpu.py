@@ -20,7 +20,9 @@ def _rand_i8(shape, seed):
 
 
 SHAPES = [(128, 256, 128), (256, 512, 384), (100, 72, 96), (1, 16, 16), (129, 257, 144), (300, 1000, 512),
-          (1024, 1024, 1024), (64, 4096, 4096), (17, 40, 50), (3, 5, 7)]
+          (1024, 1024, 1024), (64, 4096, 4096), (17, 40, 50), (3, 5, 7),
+          # enough 256x256 tiles for the CTA-pair kernel, with ragged edges
+          (2200, 2144, 512), (2304, 2304, 384), (4100, 3000, 200)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -33,7 +35,7 @@ def test_int32_accumulator_bit_exact(M, N, K, layout):
     np.testing.assert_array_equal(C.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (100, 72, 96), (512, 512, 512), (333, 160, 256)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (100, 72, 96), (512, 512, 512), (333, 160, 256), (2200, 2144, 512)])
 def test_dequant_fp16_bit_exact(M, N, K):
     g = torch.Generator().manual_seed(7 + M)
     A_fp = torch.randn(M, K, generator=g).to(torch.float16)
