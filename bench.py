@@ -362,10 +362,14 @@ def run_ours(args):
     e2e_val = FLOPS_CAUSAL * world / (e2e_ms * 1e-3) / 1e12
     nbytes = q.numel() * q.element_size()
 
+    del qh, kh, vh, oh, qd, kd, vd
+    decoder = decoder_layer_measure(args, llm_kernels, world, rank, dev)
+
     ops = {}
     cpu = None
     if rank == 0:
         ops = secondary_ops(args, llm_kernels, peaks)
+        ops["decoder_layer_config5"] = decoder
         if world == 1:
             cpu = cpu_baselines()
 
@@ -412,6 +416,31 @@ def run_ours(args):
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decoder_layer_measure(args, llm_kernels, world, rank, dev):
+    """Config 5: the Llama-7B-shaped decoder-layer op mix (RMSNorm+QKV, causal attention,
+    int8 O-proj, int8 MLP-up) on a global batch of 64 x 2048 tokens split over the ranks
+    (strong scaling: 64 / n_gpus sequences per GPU), weights N(0, 0.02), x N(0, 1) bf16."""
+    T, GB = 2048, 64
+    from llm_kernels.sharding import shard_range
+
+    s, e = shard_range(GB, rank, world)
+    g = torch.Generator().manual_seed(4)
+    layer = llm_kernels.DecoderLayerOps().to(dev)
+    layer.init_weights(g)
+    gx = torch.Generator().manual_seed(40 + rank)
+    x = torch.randn(e - s, T, 4096, generator=gx).to(torch.bfloat16).to(dev)
+    step = lambda: layer(x)  # noqa: E731
+    reps = 2 if args.quick else 4
+    ms = time_loop(step, reps, 2, world) / reps
+    fl = layer.flops(GB, T)
+    total = sum(fl.values())
+    del x, layer
+    torch.cuda.empty_cache()
+    return {"value": GB * T / (ms * 1e-3), "unit": "tokens/s", "ms_per_layer": ms,
+            "ops_per_s": total / (ms * 1e-3), "tera_ops_per_layer": {k: v / 1e12 for k, v in fl.items()},
+            "sequences_per_gpu": e - s, "scaling": "strong (global batch 64 x 2048 fixed)"}
 
 
 def secondary_ops(args, llm_kernels, peaks):

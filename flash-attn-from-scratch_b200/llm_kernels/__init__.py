@@ -112,6 +112,8 @@ class Int8Linear(nn.Module):
         return f"d_in={self.d_in}, d_out={self.d_out}"
 
 
+from .decoder import DecoderLayerOps  # noqa: E402  (uses the modules above)
+
 __all__ = [
     # functions
     "flash_attn_forward",

@@ -16,7 +16,7 @@ from ._common import dtype_code, ptr, require, require_cuda, stream_for
 __all__ = ["flash_attn_forward"]
 
 
-def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_scale=None):
+def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_scale=None, out=None):
     """``O = softmax(Q K^T * scale [+ causal mask]) V`` for ``[B, H, M, D]`` tensors.
 
     Args:
@@ -26,9 +26,12 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
         block_m, block_n : accepted for signature compatibility; the sm_100a kernel uses
             its own 128-row tiles and handles any M, N.
         softmax_scale : defaults to D**-0.5 (flash_attn_fwd.py:50)
+        out : optional preallocated ``[B, H, M, D]`` output (any strides with a contiguous
+            last dim), e.g. a ``[B, M, H, D]`` buffer viewed with ``transpose(1, 2)`` so the
+            next projection reads it without a copy.
 
     Returns:
-        out : like ``q`` (``torch.empty_like(q)``, flash_attn_fwd.py:136)
+        out : like ``q`` (``torch.empty_like(q)``, flash_attn_fwd.py:136), or ``out``
     """
     require(isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor) and isinstance(v, torch.Tensor), "q, k, v must be tensors")
     require(q.dtype in (torch.float16, torch.bfloat16) and q.is_cuda, "q must be a CUDA fp16/bf16 tensor")
@@ -42,14 +45,17 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
     require(k.shape == (B, H, N, D) and v.shape == (B, H, N, D), "k and v must be [B, H, N, D] matching q")
     require(0 < D <= 128, f"head dim {D} not supported (1..128)")
     scale = float(softmax_scale) if softmax_scale is not None else float(D) ** -0.5
+    if out is not None:
+        require(isinstance(out, torch.Tensor) and out.shape == q.shape and out.dtype == q.dtype
+                and out.device == q.device, "out must match q's shape, dtype and device")
     if D not in (64, 128):
         # The tcgen05 kernels are built for D = 64 and 128; other head dims are zero-padded
         # (zero columns add nothing to Q K^T, and the padded output columns are dropped).
         Dp = 64 if D < 64 else 128
         pad = lambda t: torch.nn.functional.pad(t, (0, Dp - D))
-        out = flash_attn_forward(pad(q), pad(k), pad(v), causal, block_m, block_n, softmax_scale=scale)
-        res = torch.empty_like(q)
-        res.copy_(out[..., :D])
+        padded = flash_attn_forward(pad(q), pad(k), pad(v), causal, block_m, block_n, softmax_scale=scale)
+        res = out if out is not None else torch.empty_like(q)
+        res.copy_(padded[..., :D])
         return res
     if q.stride(-1) != 1:
         q = q.contiguous()
@@ -57,9 +63,17 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
         k = k.contiguous()
     if v.stride(-1) != 1:
         v = v.contiguous()
-    out = torch.empty_like(q)
-    if out.stride(-1) != 1:
-        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    if out is not None and out.stride(-1) == 1 and all(s % 8 == 0 for s in out.stride()[:3]) \
+            and out.data_ptr() % 16 == 0:
+        pass
+    elif out is not None:
+        res = flash_attn_forward(q, k, v, causal, block_m, block_n, softmax_scale=scale)
+        out.copy_(res)
+        return out
+    else:
+        out = torch.empty_like(q)
+        if out.stride(-1) != 1:
+            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     if out.numel() == 0:
         return out
     require(N > 0, "flash_attn_forward: need at least one key")
