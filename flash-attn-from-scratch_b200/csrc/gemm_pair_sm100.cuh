@@ -14,7 +14,7 @@
 //              ring (~1200 cycles per slot).
 //   warp 1     TMEM owner in both CTAs (pair allocation); MMA issuer in the even CTA only:
 //              tcgen05.mma.cta_group::2, then one commit to each CTA's ring-slot barrier and,
-//              per tile, to each CTA's accumulator barrier (no multicast qualifier: the peer's
+//              per tile, to each CTA's accumulator barrier (two plain commits; the peer's
 //              barrier is addressed through mapa).
 //   warps 2-5  epilogue in both CTAs: each drains its own 128 rows x 256 columns from its TMEM
 //              and tells the even CTA (local or remote arrive) when the buffer is free.

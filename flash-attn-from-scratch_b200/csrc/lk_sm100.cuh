@@ -3,7 +3,7 @@
 // Thin inline-PTX wrappers for the Blackwell async machinery the kernels are built on:
 //   * mbarriers with BOUNDED waits (every wait gives up after a wall-clock limit, records
 //     where it gave up in the device status word and reports failure to the caller),
-//   * TMA tiled loads (cp.async.bulk.tensor, no multicast anywhere in this library),
+//   * TMA tiled loads, each into the issuing CTA's own shared memory only,
 //   * tcgen05: TMEM alloc/dealloc, MMA (kind::f16 / kind::i8 / kind::tf32), commit,
 //     TMEM loads/stores and the thread-sync fences,
 //   * UMMA shared-memory matrix descriptors and instruction descriptors.
@@ -125,7 +125,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (tiled, no multicast).  `tmap` is the address of a __grid_constant__ CUtensorMap.
+// TMA (tiled, single destination CTA).  `tmap` is the address of a __grid_constant__ CUtensorMap.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -317,8 +317,8 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt
 }
 
 // ---------------------------------------------------------------------------------------------
-// CTA pairs (cluster of 2) for tcgen05 cta_group::2.  No TMA multicast is used: each CTA of
-// the pair loads its own operand halves; only the MMA and its commit span the pair.
+// CTA pairs (cluster of 2) for tcgen05 cta_group::2.  Each CTA of the pair loads its own
+// operand halves into its own shared memory; only the MMA and its commits span the pair.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
