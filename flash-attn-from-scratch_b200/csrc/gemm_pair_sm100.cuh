@@ -20,6 +20,17 @@
 //              and tells the even CTA (local or remote arrive) when the buffer is free.
 // The pair synchronises with barrier.cluster after set-up and before TMEM is released, so no
 // CTA exits while its peer may still read its shared memory.  All mbarrier waits are bounded.
+//
+// Split tail.  When the tiles do not fill a whole number of rounds, the leftover tiles (fewer
+// than the pairs) are cut along K into `split` parts, and those parts are every pair's FIRST
+// unit, so the partial round trip overlaps the pair's next tile (the accumulator is double
+// buffered) instead of ending the kernel.  Per warp slot (32 rows x 256 columns) the parts meet
+// in the epilogue: each takes a ticket from an arrival counter; the first split-1 tickets write
+// their raw accumulator to a workspace and publish it (one fence, one counter bump); the last
+// ticket adds those partials to its own accumulator and runs the op's epilogue.  It waits only
+// on parts that already hold a ticket, i.e. are running, so no residency assumption is made;
+// it re-zeroes the counters for the next launch.  Integer partial sums are exact, so the int8
+// result is bit-identical to the unsplit one.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -41,7 +52,10 @@ struct PairConfig {
   static constexpr int kBBoxes = kBMN ? (kHalfN * KT::kElemBytes) / 128 : 1;
   static constexpr int kBBoxBytes = kBMN ? kBK * 128 : kBBytes;
   static constexpr int kTmemCols = 2 * kBN;  // double-buffered 256-column accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSbStageBytes = 4 * 256 * 4;  // per epilogue warp: the tile's 256 column scales
+  // Per epilogue warp: two 2 KB store tiles of 32 rows x 64 bytes (64-byte swizzle) for TMA stores of C.
+  static constexpr int kCStageBytes = 4 * 2 * 2048;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kCStageBytes + 1024 + 256 + kSbStageBytes;
   static constexpr uint32_t kIdesc =
       make_idesc(KT::kCFmt, KT::kAFmt, KT::kBFmt, 0u, kBMN ? 1u : 0u, 2u * kBM, (uint32_t)kBN);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -53,12 +67,38 @@ enum PairSite : int {
   kSitePairFull = 123,
   kSitePairAccFull = 124,
   kSitePairTeardown = 125,
+  kSitePairSplit = 126,
 };
+
+struct Unit {
+  int tile, kb0, kb1, part;  // part < 0: the whole tile
+};
+
+// Units [0, tail units) are the split parts of tiles full_tiles.. (so every pair with one
+// starts with it); the rest are the whole tiles 0..full_tiles-1 in raster order.
+__device__ __forceinline__ Unit decode_unit(int u, const Params& p, int num_kb) {
+  Unit w;
+  const int tail_units = p.split > 1 ? (p.num_tiles - p.full_tiles) * p.split : 0;
+  if (u >= tail_units) {
+    w.tile = u - tail_units;
+    w.kb0 = 0;
+    w.kb1 = num_kb;
+    w.part = -1;
+    return w;
+  }
+  const int v = u;
+  const int tail = v / p.split;
+  w.part = v - tail * p.split;
+  w.tile = p.full_tiles + tail;
+  w.kb0 = (int)((int64_t)num_kb * w.part / p.split);
+  w.kb1 = (int)((int64_t)num_kb * (w.part + 1) / p.split);
+  return w;
+}
 
 template <Kind kKind, bool kBMN, Epi kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const Params p) {
+                     const __grid_constant__ CUtensorMap tmC, const Params p) {
   using Cfg = PairConfig<kKind, kBMN>;
   using KT = typename Cfg::KT;
   constexpr int S = Cfg::kStages;
@@ -68,7 +108,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* c_stage = smem + S * Cfg::kStageBytes;  // [4 warps][2][32 rows x 64 B], 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(c_stage + Cfg::kCStageBytes);
   uint64_t* full = bars;               // [S]  (even CTA's copy used) both CTAs' TMA bytes -> MMA
   uint64_t* empty = bars + S;          // [S]  MMA commit -> each CTA's producer
   uint64_t* acc_full = bars + 2 * S;   // [2]  MMA commit -> each CTA's epilogue
@@ -76,6 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* sb_stage = reinterpret_cast<float*>(c_stage + Cfg::kCStageBytes + 256);  // [4 warps][256]
 
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
@@ -100,6 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.c_tma) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
@@ -118,12 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+      for (int u = pair; u < p.num_units && ok; u += npairs) {
+        const Unit w = decode_unit(u, p, num_kb);
         int mb, nb;
-        tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb);
         const int m0 = mb * kPairM + (int)rank * kBM;
         const int n0 = nb * Cfg::kBN + (int)rank * Cfg::kHalfN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, kSitePairEmpty) || *(volatile int*)abort_flag) {
             ok = false;
             break;
@@ -159,7 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int t = pair; t < p.num_tiles && ok; t += npairs, ++local) {
+      for (int u = pair; u < p.num_units && ok; u += npairs, ++local) {
+        const Unit w = decode_unit(u, p, num_kb);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
@@ -168,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kBN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&full[stage], phase, kSitePairFull)) {
             ok = false;
             break;
@@ -185,9 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               bdesc = sdesc_sw128(b_base + ks * 32, 16, 1024);
             if constexpr (kKind == Kind::I8)
-              mma_i8_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb | ks) != 0);
+              mma_i8_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
             else
-              mma_f16_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb | ks) != 0);
+              mma_f16_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
           }
           tc_commit_pair(cluster_addr(&empty[stage], 0));
           tc_commit_pair(cluster_addr(&empty[stage], 1));
@@ -208,16 +253,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (both)
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
+    const int wslot = (int)rank * 4 + quad;  // this warp's 32 rows of the pair tile
+    const int nwriters = p.split - 1;
+    int* arrive_ctr = p.split_flags;                                    // [tail tiles][8]
+    int* ready_ctr = p.split_flags + (p.num_tiles - p.full_tiles) * 8;  // [tail writers][8]
+    float* my_sb = sb_stage + (warp - 2) * 256;
+    uint8_t* my_cst = c_stage + (warp - 2) * 4096;
+    int cbuf = 0;  // next store tile of this warp
     int local = 0;
-    for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+    for (int u = pair; u < p.num_units; u += npairs, ++local) {
+      const Unit w = decode_unit(u, p, num_kb);
       int mb, nb;
-      tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb);
       const int m = mb * kPairM + (int)rank * kBM + row_in_tile;
+      const int m_warp = m - lane;  // first row of this warp's 32
       const int n_base = nb * Cfg::kBN;
       const bool row_ok = m < p.M;
       float row_scale = 0.f;
       if constexpr (kEpi == Epi::DequantF16) {
         row_scale = row_ok ? __ldg(p.sa + m) : 0.f;
+        // The tile's column scales go to this warp's shared slice while the MMAs run, so the
+        // chunk loop below reads them without a round trip to L2.  (The warp finished reading
+        // the previous tile's slice before it got here.)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = n_base + i * 32 + lane;
+          my_sb[i * 32 + lane] = n < p.N ? __ldg(p.sb + n) : 0.f;
+        }
+        __syncwarp();
       } else if constexpr (kEpi == Epi::RowRsqrt) {
         if (local == 0) griddep_wait();
         row_scale = row_ok ? __ldcg(p.rstd + m) : 0.f;
@@ -227,12 +290,106 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSitePairAccFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * Cfg::kBN);
+      // Split-tail role of this warp slot: a ticket below nwriters writes its partial, the
+      // last ticket finishes the tile.
+      const int tail = w.tile - p.full_tiles;
+      int ticket = -1;
+      if (w.part >= 0) {
+        if (lane == 0) ticket = atomicAdd(arrive_ctr + tail * 8 + wslot, 1);
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      }
+      const bool writer = ticket >= 0 && ticket < nwriters;
+      const bool finisher = ticket >= 0 && !writer;
+      bool ok = true;
+      if (finisher) {
+        for (int wi = 0; wi < nwriters; ++wi) {
+          int good = 1;
+          if (lane == 0) good = wait_counter_gt(ready_ctr + (tail * nwriters + wi) * 8 + wslot, 0, kSitePairSplit);
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) ok = false;
+        }
+        __syncwarp();
+      }
+      const int widx = writer ? tail * nwriters + ticket : 0;
+
+      // One 32-column chunk, its accumulator in r.
+      auto process = [&](int c, uint32_t (&r)[32]) {
+        if (writer) {
+          // Chunk layout [8 x 32 lanes] of uint4: every store instruction writes 512 contiguous bytes.
+          uint4* dst = p.split_partial + ((size_t)(widx * 8 + wslot) * 8 + c) * 256 + lane;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j * 32] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          return;
+        }
+        if (!ok) return;
+        if (finisher) {
+          for (int wi = 0; wi < nwriters; ++wi) {
+            const uint4* src =
+                p.split_partial + ((size_t)((tail * nwriters + wi) * 8 + wslot) * 8 + c) * 256 + lane;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 q = __ldcg(src + j * 32);
+              if constexpr (kKind == Kind::I8) {
+                r[4 * j + 0] += q.x;
+                r[4 * j + 1] += q.y;
+                r[4 * j + 2] += q.z;
+                r[4 * j + 3] += q.w;
+              } else {
+                r[4 * j + 0] = __float_as_uint(__uint_as_float(r[4 * j + 0]) + __uint_as_float(q.x));
+                r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + __uint_as_float(q.y));
+                r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + __uint_as_float(q.z));
+                r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + __uint_as_float(q.w));
+              }
+            }
+          }
+        }
+        const int n0 = n_base + c * 32;
+        if (n0 >= p.N || m_warp >= p.M) return;
+        if (!p.c_tma) {
+          if (row_ok) store_chunk<kKind, kEpi>(r, row_scale, m, n0, p, my_sb + c * 32);
+          return;
+        }
+        // Staged store: each lane writes its row's 64-byte pieces into a 32-row tile (64-byte
+        // swizzle: 16-byte piece q of row r at q ^ ((r >> 1) & 3), conflict-free), then lane 0
+        // stores the tile with TMA; rows past M and columns past N are clipped by the copy.
+        uint4 wv[8];
+        pack_chunk<kKind, kEpi>(r, row_scale, p, my_sb + c * 32, wv);
+        constexpr int kPieces = (kEpi == Epi::RawI32) ? 2 : 1;  // 64-byte tiles per chunk
+        constexpr int kColsPerPiece = (kEpi == Epi::RawI32) ? 16 : 32;
+#pragma unroll
+        for (int h = 0; h < kPieces; ++h) {
+          const int x = n0 + h * kColsPerPiece;
+          if (x >= p.N) break;
+          if (lane == 0) bulk_wait_group_read<1>();  // the tile's previous store has read it
+          __syncwarp();
+          uint8_t* tile = my_cst + cbuf * 2048;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(tile + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = wv[h * 4 + q];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, tile, x, m_warp);
+            bulk_commit_group();
+          }
+          cbuf ^= 1;
+        }
+      };
+
+      // TMEM loads run one chunk ahead of the processing; the buffer is handed back to the MMA
+      // warp as soon as the last chunk is in registers.
+      constexpr int kChunks = Cfg::kBN / 32;
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_row, ra);
+      tmem_wait_ld_regs(ra);
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tmem_wait_ld();
-        if (c == Cfg::kBN / 32 - 1) {
+      for (int c = 0; c < kChunks; c += 2) {
+        tmem_ld32(t_row + (c + 1) * 32, rb);
+        process(c, ra);
+        tmem_wait_ld_regs(rb);
+        if (c + 2 < kChunks) {
+          tmem_ld32(t_row + (c + 2) * 32, ra);
+        } else {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -242,12 +399,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_remote(&acc_empty[acc], 0);
           }
         }
-        const int n0 = n_base + c * 32;
-        if (!row_ok || n0 >= p.N) continue;
-        store_chunk<kKind, kEpi>(r, row_scale, m, n0, p);
+        process(c + 1, rb);
+        if (c + 2 < kChunks) tmem_wait_ld_regs(ra);
       }
+      if (writer) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(ready_ctr + widx * 8 + wslot, 1);
+      }
+      if (!ok) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      if (finisher && lane == 0) {
+        // Every part holds a ticket and every writer has published its partial: reset for the
+        // next launch on this workspace.
+        arrive_ctr[tail * 8 + wslot] = 0;
+        for (int wi = 0; wi < nwriters; ++wi) ready_ctr[(tail * nwriters + wi) * 8 + wslot] = 0;
+      }
+      __syncwarp();
       if (*(volatile int*)abort_flag) break;
     }
+    if (lane == 0) bulk_wait_group<0>();  // C stores complete before the CTA's shared memory goes
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -258,7 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <Kind kKind, bool kBMN, Epi kEpi>
-int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Params& p, int num_sms, cudaStream_t stream) {
+int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const Params& p, int num_sms,
+                cudaStream_t stream) {
   using Cfg = PairConfig<kKind, kBMN>;
   auto kern = gemm_pair_kernel<kKind, kBMN, kEpi>;
   static std::atomic<uint64_t> configured{0};
@@ -285,7 +460,7 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Params& p,
   attr[1].val.programmaticStreamSerializationAllowed = (kEpi == Epi::RowRsqrt) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
 }
 
 }  // namespace gemm

@@ -49,6 +49,13 @@ struct Params {
   const float* sa;  // DequantF16
   const float* sb;
   const float* rstd;  // RowRsqrt: per-row rsqrt(mean(x^2)+eps) from the programmatic predecessor
+  // CTA-pair kernel only: work units.  Units below full_tiles are whole tiles; the remaining
+  // (num_tiles - full_tiles) tail tiles are each cut into `split` K ranges so the last round
+  // occupies every pair.  split <= 1 means no split (num_units = num_tiles).
+  int full_tiles, split, num_units;
+  uint4* split_partial;  // [tail writers][8 warp slots][8 chunks][8][32] partial accumulators
+  int c_tma;             // CTA-pair kernel: C is written by TMA stores through the tmC map
+  int* split_flags;      // [tail tiles x 8] arrival counters, then [tail writers x 8] chunk counters
 };
 
 constexpr int kBM = 128;
@@ -127,9 +134,49 @@ __device__ __forceinline__ uint32_t pack_bf162(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Epilogue values of one 32-column chunk of an accumulator row.  `sbp` points at the column
+// scales of the chunk (DequantF16 only; global or shared memory); with vec_sb they are read as
+// eight 16-byte vectors, otherwise one by one up to column N.
+template <Kind kKind, Epi kEpi>
+__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], float row_scale, int n0, const Params& p,
+                                             const float* sbp, bool vec_sb, float (&v)[32]) {
+  if constexpr (kEpi == Epi::DequantF16) {
+    // Bit-exact order of the reference epilogue: (fp32(acc) * sa[m]) * sb[n].
+    if (vec_sb) {
+      const float4* sb4 = reinterpret_cast<const float4*>(sbp);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 s4 = sb4[j];
+        v[4 * j + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 0]), row_scale), s4.x);
+        v[4 * j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 1]), row_scale), s4.y);
+        v[4 * j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 2]), row_scale), s4.z);
+        v[4 * j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 3]), row_scale), s4.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float sbj = (n0 + j < p.N) ? sbp[j] : 0.f;
+        v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), row_scale), sbj);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
+  }
+}
+
+template <Kind kKind, Epi kEpi>
+__device__ __forceinline__ uint32_t pack_out2(float a, float b) {
+  if constexpr (kEpi == Epi::RowRsqrt && kKind == Kind::BF16)
+    return pack_bf162(a, b);
+  else
+    return pack_half2(a, b);
+}
+
 // Stores one 32-column chunk of accumulator row m (columns n0..n0+31) with the op's epilogue.
 template <Kind kKind, Epi kEpi>
-__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_scale, int m, int n0, const Params& p) {
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_scale, int m, int n0, const Params& p,
+                                            const float* sbp) {
   const bool full_chunk = (n0 + 32 <= p.N);
   if constexpr (kEpi == Epi::RawI32) {
     int32_t* crow = static_cast<int32_t*>(p.C) + (int64_t)m * p.ldc + n0;
@@ -144,44 +191,17 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_s
     }
   } else {
     float v[32];
-    if constexpr (kEpi == Epi::DequantF16) {
-      // Bit-exact order of the reference epilogue: (fp32(acc) * sa[m]) * sb[n].
-      const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0);
-      if (full_chunk && ((reinterpret_cast<uintptr_t>(p.sb + n0) & 15) == 0)) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 s4 = __ldg(sb4 + j);
-          v[4 * j + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 0]), row_scale), s4.x);
-          v[4 * j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 1]), row_scale), s4.y);
-          v[4 * j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 2]), row_scale), s4.z);
-          v[4 * j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[4 * j + 3]), row_scale), s4.w);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sbj = (n0 + j < p.N) ? __ldg(p.sb + n0 + j) : 0.f;
-          v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), row_scale), sbj);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
-    }
+    chunk_values<kKind, kEpi>(r, row_scale, n0, p, sbp,
+                              full_chunk && ((reinterpret_cast<uintptr_t>(sbp) & 15) == 0), v);
     uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
     constexpr bool kBf16Out = (kEpi == Epi::RowRsqrt && kKind == Kind::BF16);
     if (full_chunk && (p.ldc % 8 == 0)) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 w;
-        if constexpr (kBf16Out) {
-          w = make_uint4(pack_bf162(v[8 * j], v[8 * j + 1]), pack_bf162(v[8 * j + 2], v[8 * j + 3]),
-                         pack_bf162(v[8 * j + 4], v[8 * j + 5]), pack_bf162(v[8 * j + 6], v[8 * j + 7]));
-        } else {
-          w = make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
-                         pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
-        }
-        reinterpret_cast<uint4*>(crow)[j] = w;
-      }
+      for (int j = 0; j < 4; ++j)
+        reinterpret_cast<uint4*>(crow)[j] =
+            make_uint4(pack_out2<kKind, kEpi>(v[8 * j], v[8 * j + 1]), pack_out2<kKind, kEpi>(v[8 * j + 2], v[8 * j + 3]),
+                       pack_out2<kKind, kEpi>(v[8 * j + 4], v[8 * j + 5]),
+                       pack_out2<kKind, kEpi>(v[8 * j + 6], v[8 * j + 7]));
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -192,6 +212,25 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_s
           crow[j] = __half_as_ushort(__float2half_rn(v[j]));
       }
     }
+  }
+}
+
+// The chunk as 16-byte words of the output type (4 for 16-bit outputs, 8 for int32), for a
+// staged store.  sbp: 32 scales, 16-byte aligned, zero past column N.
+template <Kind kKind, Epi kEpi>
+__device__ __forceinline__ void pack_chunk(const uint32_t (&r)[32], float row_scale, const Params& p, const float* sbp,
+                                           uint4 (&w)[8]) {
+  if constexpr (kEpi == Epi::RawI32) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+  } else {
+    float v[32];
+    chunk_values<kKind, kEpi>(r, row_scale, 0, p, sbp, true, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = make_uint4(pack_out2<kKind, kEpi>(v[8 * j], v[8 * j + 1]), pack_out2<kKind, kEpi>(v[8 * j + 2], v[8 * j + 3]),
+                        pack_out2<kKind, kEpi>(v[8 * j + 4], v[8 * j + 5]),
+                        pack_out2<kKind, kEpi>(v[8 * j + 6], v[8 * j + 7]));
   }
 }
 
@@ -389,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int n0 = n_base + c * 32;
         if (!row_ok || n0 >= p.N) continue;
-        store_chunk<kKind, kEpi>(r, row_scale, m, n0, p);
+        store_chunk<kKind, kEpi>(r, row_scale, m, n0, p, kEpi == Epi::DequantF16 ? p.sb + n0 : nullptr);
       }
       if (*(volatile int*)abort_flag) break;
     }

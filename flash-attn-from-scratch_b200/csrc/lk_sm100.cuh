@@ -58,6 +58,30 @@ __device__ __forceinline__ bool device_failed() {
   return *(volatile int*)&g_status[0] != 0;
 }
 
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until the global counter *ctr exceeds `value` (acquire).  Used only on
+// counters whose writer has already announced itself running, so the wait is short.
+__device__ __forceinline__ bool wait_counter_gt(const int* ctr, int value, int site) {
+  if (ld_acquire_gpu(ctr) > value) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (ld_acquire_gpu(ctr) <= value) {
+    if ((++spins & 63u) == 0) {
+      if (device_failed()) return false;
+      if (globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
+        record_failure(kDevTimeout, site);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Shared-memory address helpers
 // ---------------------------------------------------------------------------------------------
@@ -157,6 +181,27 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// TMA tiled store shared -> global (bulk-group completion).  Elements of the box outside the
+// tensor are not written, so ragged edges need no special case.  The innermost coordinate c0
+// times the element size must be a multiple of 16 bytes, and c0, c1 must not be negative.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N committed bulk groups of this thread are incomplete (writes done).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -252,6 +297,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// tcgen05.wait::ld that also names the 32 destination registers of the load it waits for, so
+// the compiler cannot move any use of them above the wait (needed when a second load is in
+// flight while the first one's registers are consumed).
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
 }
 
 // 32 lanes x 16 consecutive 32-bit columns.

@@ -35,7 +35,10 @@ def test_int32_accumulator_bit_exact(M, N, K, layout):
     np.testing.assert_array_equal(C.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (100, 72, 96), (512, 512, 512), (333, 160, 256), (2200, 2144, 512)])
+# (2304, 2300, *): CTA-pair kernel with a C row pitch that is not a multiple of 16 bytes, so C
+# is stored directly instead of through TMA tiles (unsplit, and split 4 ways along K).
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (100, 72, 96), (512, 512, 512), (333, 160, 256), (2200, 2144, 512),
+                                   (2304, 2300, 1024), (2304, 2300, 4096)])
 def test_dequant_fp16_bit_exact(M, N, K):
     g = torch.Generator().manual_seed(7 + M)
     A_fp = torch.randn(M, K, generator=g).to(torch.float16)
@@ -48,6 +51,45 @@ def test_dequant_fp16_bit_exact(M, N, K):
     np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref.view(np.uint16))
     C2 = llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb)
     np.testing.assert_array_equal(C2.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+# Shapes whose leftover 256x256 tiles the CTA-pair kernel splits along K into 2, 3 and 4 parts
+# (7, 23 and 7 left over of 81, 171 and 81 tiles on 74 pairs), with ragged edges.
+SPLIT_SHAPES = [(2200, 2144, 2048), (2304, 4864, 3072), (2200, 2144, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+def test_split_tail_bit_exact(M, N, K, layout):
+    A = _rand_i8((M, K), 11 + M)
+    B = _rand_i8((K, N) if layout == "kn" else (N, K), 12 + N)
+    Ad, Bd = A.cuda(), B.cuda()
+    ref = oracle.int8_gemm_i32(A.numpy(), B.numpy(), layout)
+    C = llm_kernels.int8_gemm_i32(Ad, Bd, layout)
+    np.testing.assert_array_equal(C.cpu().numpy(), ref)
+    # the split counters are re-armed by each launch: a second launch on the same stream, after
+    # one of another shape, and one on a side stream agree bit for bit
+    llm_kernels.int8_gemm_i32(Ad[:, : K // 2].contiguous(), Bd[: K // 2].contiguous() if layout == "kn"
+                              else Bd[:, : K // 2].contiguous(), layout)
+    C2 = llm_kernels.int8_gemm_i32(Ad, Bd, layout)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        C3 = llm_kernels.int8_gemm_i32(Ad, Bd, layout)
+    torch.cuda.current_stream().wait_stream(side)
+    assert torch.equal(C2, C) and torch.equal(C3, C)
+
+
+def test_split_tail_dequant_fp16_bit_exact():
+    M, N, K = 2304, 4864, 3072
+    g = torch.Generator().manual_seed(21)
+    A_q, sa = llm_kernels.quantize_symmetric(torch.randn(M, K, generator=g).to(torch.float16).cuda())
+    B_q, sb = llm_kernels.quantize_symmetric(torch.randn(N, K, generator=g).to(torch.float16).cuda())
+    ref = oracle.int8_gemm_dequant(A_q.cpu().numpy(), B_q.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy(), "nk")
+    C = llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb)
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+    C_kn = llm_kernels.int8_gemm_dequant_fwd(A_q, B_q.T.contiguous(), sa, sb)
+    np.testing.assert_array_equal(C_kn.cpu().numpy().view(np.uint16), ref.view(np.uint16))
 
 
 def test_golden_vectors_from_reference_kernel():
@@ -75,9 +117,16 @@ def test_full_size_4096_cubed():
     rows = slice(1024, 1280)
     ref = oracle.int8_gemm_i32(A_q[rows].cpu().numpy(), B_q.cpu().numpy(), "nk")
     np.testing.assert_array_equal(acc[rows].cpu().numpy(), ref)
+    # the 34 tiles left over after 3 rounds of 74 pairs (split along K): M-blocks 14-15 from
+    # N-block 11, M-blocks 8-15 of N-blocks 12-15, all inside rows 2048.. and columns 2816..
+    ref_tail = oracle.int8_gemm_i32(A_q[2048:].cpu().numpy(), B_q[2816:].cpu().numpy(), "nk")
+    np.testing.assert_array_equal(acc[2048:, 2816:].cpu().numpy(), ref_tail)
     lhs = acc.to(torch.int64).sum(1)
     rhs = (A_q.to(torch.int64) * B_q.to(torch.int64).sum(0)[None, :]).sum(1)
     assert torch.equal(lhs, rhs)
+    col_lhs = acc.to(torch.int64).sum(0)
+    col_rhs = (B_q.to(torch.int64) * A_q.to(torch.int64).sum(0)[None, :]).sum(1)
+    assert torch.equal(col_lhs, col_rhs)
     C = llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb)
     refC = oracle.dequant_f16(acc.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy())
     np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), refC.view(np.uint16))
