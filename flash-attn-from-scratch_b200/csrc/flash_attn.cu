@@ -10,19 +10,21 @@
 // CTA = one (batch, head) and 256 query rows held as two 128-row tiles (t = 0, 1).  10 warps:
 //   warps 0-3  softmax for tile 0 (thread = one query row = one TMEM lane)
 //   warps 4-7  softmax for tile 1
-//   warp  8    TMA producer: Q0/Q1 once, then K_0, K_1, V_0, K_2, V_1, ... (consumption
-//              order) through a ring of 128-row stages (128B swizzle)
+//   warp  8    TMA producer: Q0/Q1 once, then K_0, V_0, K_1, V_1, ... (consumption order)
+//              through a ring of 128-row stages (128B swizzle)
 //   warp  9    TMEM owner + single-thread MMA issuer
 // Tensor memory (512 columns): S_t = cols [128t, 128t+128) fp32, O_t = cols
-// [256 + D*t, 256 + D*(t+1)) fp32.  P_t goes to shared memory (K-major, 128B swizzle) so the
-// PV product is a shared-memory x shared-memory MMA: on B200 an M128 N128 K16 MMA whose A
-// comes from TMEM costs ~115 cycles against ~77 with both operands in shared memory.
-// Since S_t no longer holds P, S for key block j+1 is issued as soon as the softmax of block
-// j has read S_t(j) into registers; per block j the MMA order is S0(j+1), S1(j+1), PV0(j),
-// PV1(j), which keeps the tensor core fed while the softmax of block j runs.
+// [256 + D*t, 256 + D*(t+1)) fp32.  P_t (the input dtype, two per column) overwrites the first
+// 64 columns of S_t once the softmax has S_t(j) in registers, and the PV product takes its A
+// operand from tensor memory (an M128 N128 K16 MMA costs the same 64 cycles with A in TMEM or
+// in shared memory), so shared memory holds only Q and a deep K/V ring.
+// Per tile the MMA warp issues PV_t(j) and then S_t(j+1) as soon as P_t(j) is ready: the
+// tensor pipe executes a thread's MMAs in order, so S_t(j+1) overwrites P_t(j) only after
+// PV_t(j) has read it, and when S_t(j+1) is complete PV_t(j) is too -- the softmax of block
+// j+1 may then rescale O_t in place with no further wait.  The two tiles interleave, so the
+// tensor core multiplies one tile while the other tile's softmax runs.
 // Rescaling is lazy: the running max used for exp2 only moves when the block max exceeds it
-// by more than 8 (log2 units), so P <= 256 and O is rarely touched; the softmax warps do it
-// themselves once PV_t(j-1) has completed.
+// by more than 8 (log2 units), so P <= 256 and O is rarely touched.
 // Every mbarrier wait is bounded; on failure all roles unwind and TMEM is freed.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -47,6 +49,15 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #define LK_FA_GROUP_HEADS 1  // 0: one global heavy-first order over all heads
 #endif
 constexpr int kPolyPairs = LK_FA_POLY_PAIRS;  // of every 16 exp2 pairs, this many on the FMA pipe
+// The two tiles take turns on the exp phase: measured faster at D = 128 (where the exp phase
+// is on each tile's critical chain), slower at D = 64.  -1 = per head dim, 0/1 = off/on.
+#ifndef LK_FA_EXP_TURNS
+#define LK_FA_EXP_TURNS -1
+#endif
+template <int D>
+__host__ __device__ constexpr bool exp_turns() {
+  return LK_FA_EXP_TURNS < 0 ? (D == 128) : (LK_FA_EXP_TURNS != 0);
+}
 
 enum Site : int {
   kSiteLoadQ = 201,
@@ -73,13 +84,13 @@ template <int D>
 struct Cfg {
   static constexpr int kQBoxes = D / 64;               // 64-element (128 B) boxes per row
   static constexpr int kTileBytes = kTileM * D * 2;    // one 128-row tile of Q, K or V
-  static constexpr int kPBytes = kTileM * kBlockN * 2; // one tile's P (32 KB)
-  static constexpr int kFixedBytes = 2 * kTileBytes + 2 * kPBytes;
+  static constexpr int kFixedBytes = 2 * kTileBytes;   // Q_0, Q_1
   static constexpr int kBudget = 232448 - 1024 - 512;  // opt-in smem - align slack - barriers
-  static constexpr int kStages = (kBudget - kFixedBytes) / kTileBytes;  // 3 (D=128) / 8 (D=64)
+  static constexpr int kFit = (kBudget - kFixedBytes) / kTileBytes;
+  static constexpr int kStages = kFit > 10 ? 10 : kFit;  // 5 (D=128) / 10 (D=64)
   static constexpr int kSmemBytes = kFixedBytes + kStages * kTileBytes + 1024 + 512;
   static constexpr int kOCol0 = 256;
-  static_assert(kStages >= 3, "K/V ring needs three stages");
+  static_assert(kStages >= 4, "K/V ring needs four stages");
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -163,23 +174,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<D>;
   constexpr int S = C::kStages;
+  constexpr bool kExpTurns = exp_turns<D>();
   constexpr uint32_t kIdescS = make_idesc(1, kBf16 ? 1 : 0, kBf16 ? 1 : 0, 0, 0, kTileM, kBlockN);
   constexpr uint32_t kIdescO = make_idesc(1, kBf16 ? 1 : 0, kBf16 ? 1 : 0, 0, 1, kTileM, D);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                  // [2][kTileBytes]
-  uint8_t* sP = smem + 2 * C::kTileBytes;              // [2][kPBytes]
-  uint8_t* sRing = sP + 2 * C::kPBytes;                // [S][kTileBytes]
+  uint8_t* sQ = smem;                          // [2][kTileBytes]
+  uint8_t* sRing = smem + 2 * C::kTileBytes;   // [S][kTileBytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + S * C::kTileBytes);
   uint64_t* q_full = bars;             // [1]
   uint64_t* kv_full = bars + 1;        // [S]   TMA -> MMA
   uint64_t* kv_empty = kv_full + S;    // [S]   MMA -> TMA (tcgen05.commit)
-  uint64_t* s_full = kv_empty + S;     // [2]   S_t(j) in TMEM (tcgen05.commit)
-  uint64_t* s_free = s_full + 2;       // [2]   softmax_t has S_t(j) in registers (4 warp arrivals)
-  uint64_t* p_full = s_free + 2;       // [2]   P_t(j) in smem, O_t rescaled (4 warp arrivals)
-  uint64_t* pv_done = p_full + 2;      // [2]   PV_t(j) finished: P_t smem free, O_t stable
-  uint64_t* exp_tok = pv_done + 2;     // [2]   exp_tok[t]: the other tile finished an exp phase
+  uint64_t* s_full = kv_empty + S;     // [2]   S_t(j) in TMEM, PV_t(j-1) complete (tcgen05.commit)
+  uint64_t* p_full = s_full + 2;       // [2]   P_t(j) in TMEM, O_t rescaled (4 warp arrivals)
+  uint64_t* o_full = p_full + 2;       // [2]   last PV_t complete (tcgen05.commit)
+  uint64_t* exp_tok = o_full + 2;      // [2]   exp_tok[t]: the other tile finished an exp phase
   uint64_t* drain = exp_tok + 2;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       nb[t] = nkb;
     }
   }
-  const int J = max(nb[0], nb[1]);
+  const int J = max(nb[0], nb[1]);  // key blocks loaded (tile 0 always has rows: nb[0] >= 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -223,9 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
-      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_full[t], 1);
       mbar_init(&exp_tok[t], 4);
     }
     mbar_init(drain, 1);
@@ -254,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < ntiles; ++t)
         for (int x = 0; x < C::kQBoxes; ++x)
           tma_load_4d(sQ + t * C::kTileBytes + x * (kTileM * 128), &tmQ, q_full, 64 * x, q0 + t * kTileM, h, b);
+      // Ring order = MMA consumption order: item 2j = K_j, item 2j+1 = V_j.
       int issued = 0;
       for (int i = 0; i < 2 * J && ok; ++i) {
         const int slot = i % S;
@@ -263,25 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&kv_full[slot], C::kTileBytes);
-        // Ring order = MMA consumption order: K_0, then (K_{j+1}, V_j) for each j, S running
-        // one key block ahead of PV.
-        bool is_v;
-        int blk;
-        if (i == 0) {
-          is_v = false;
-          blk = 0;
-        } else if ((i & 1) && (i + 1) / 2 < J) {
-          is_v = false;
-          blk = (i + 1) / 2;
-        } else if (i & 1) {
-          is_v = true;
-          blk = J - 1;
-        } else {
-          is_v = true;
-          blk = (i - 2) / 2;
-        }
-        const CUtensorMap* tm = is_v ? &tmV : &tmK;
-        const int row = blk * kBlockN;
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+        const int row = (i >> 1) * kBlockN;
         uint8_t* dst = sRing + slot * C::kTileBytes;
         for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, h, b);
         issued = i + 1;
@@ -295,36 +288,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, kSiteMmaQ);
-      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + C::kTileBytes)};
-      auto item_addr = [&](int i) { return smem_u32(sRing + (i % S) * C::kTileBytes); };
+      // Descriptors are built once and advanced with sdesc_add inside the issue loops, so an
+      // MMA costs the single issuing thread a few instructions.
+      const uint64_t q_desc[2] = {sdesc_sw128(smem_u32(sQ), 16, 1024), sdesc_sw128(smem_u32(sQ + C::kTileBytes), 16, 1024)};
+      const uint64_t ring_k_desc = sdesc_sw128(smem_u32(sRing), 16, 1024);
+      const uint64_t ring_v_desc = sdesc_sw128(smem_u32(sRing), kTileM * 128, 1024);
       auto wait_item = [&](int i) { return mbar_wait(&kv_full[i % S], (i / S) & 1, kSiteMmaKV); };
       auto release_item = [&](int i) { tc_commit(&kv_empty[i % S]); };
-      auto k_item = [&](int blk) { return blk == 0 ? 0 : 2 * blk - 1; };
-      auto v_item = [&](int blk) { return min(2 * blk + 2, 2 * J - 1); };
       // S_t = Q_t K^T : K-major A (Q) and B (K), K = D in steps of 16.
       auto issue_s = [&](int t, int blk) {
-        const uint32_t kb = item_addr(k_item(blk));
+        const uint64_t kd = sdesc_add(ring_k_desc, ((2 * blk) % S) * C::kTileBytes);
         const uint32_t d_tmem = tmem + t * kBlockN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t off = (ks >> 2) * (kTileM * 128) + (ks & 3) * 32;
-          mma_f16_ss(d_tmem, sdesc_sw128(q_addr[t] + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), kIdescS,
-                     ks > 0);
+          mma_f16_ss(d_tmem, sdesc_add(q_desc[t], off), sdesc_add(kd, off), kIdescS, ks > 0);
         }
         tc_commit(&s_full[t]);
       };
-      // O_t (+)= P_t V : A = P_t from smem (K-major, 128B swizzle), B = V MN-major.
+      // O_t (+)= P_t V : A = P_t from TMEM (columns [128t, 128t+64), two keys per column),
+      // B = V MN-major from shared memory.
       auto issue_pv = [&](int t, int blk) {
-        const uint32_t vb = item_addr(v_item(blk));
+        const uint64_t vd = sdesc_add(ring_v_desc, ((2 * blk + 1) % S) * C::kTileBytes);
         const uint32_t o_tmem = tmem + C::kOCol0 + t * D;
-        const uint32_t pb = smem_u32(sP + t * C::kPBytes);
+        const uint32_t p_tmem = tmem + t * kBlockN;
 #pragma unroll
-        for (int ks = 0; ks < kBlockN / 16; ++ks) {
-          const uint32_t poff = (ks >> 2) * (kTileM * 128) + (ks & 3) * 32;
-          mma_f16_ss(o_tmem, sdesc_sw128(pb + poff, 16, 1024), sdesc_sw128(vb + ks * 16 * 128, kTileM * 128, 1024),
-                     kIdescO, (blk > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc_commit(&pv_done[t]);
+        for (int ks = 0; ks < kBlockN / 16; ++ks)
+          mma_f16_ts(o_tmem, p_tmem + ks * 8, sdesc_add(vd, ks * 16 * 128), kIdescO, (blk > 0 || ks > 0) ? 1u : 0u);
       };
       // Prologue: S_t(0) for both tiles.
       if (ok && (ok = wait_item(0))) {
@@ -334,29 +324,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         release_item(0);
       }
       for (int j = 0; j < J && ok; ++j) {
-        // S for key block j+1 runs ahead of PV for block j: it only needs the softmax of
-        // block j to have read S_t(j) out of TMEM.
-        if (j + 1 < J) {
-          if (!wait_item(k_item(j + 1))) {
-            ok = false;
-            break;
-          }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j + 1 >= nb[t]) continue;
-            if (!mbar_wait(&s_free[t], j & 1, kSiteMmaP)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, j + 1);
-          }
-          if (!ok) break;
-          release_item(k_item(j + 1));
-        }
-        if (!wait_item(v_item(j))) {
+        if (!wait_item(2 * j + 1)) {  // V_j
           ok = false;
           break;
         }
+        tc_fence_after();
+        bool k_next = false;  // K_{j+1} is in (and used by this iteration)
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= nb[t]) continue;
           if (!mbar_wait(&p_full[t], j & 1, kSiteMmaP)) {
@@ -365,9 +338,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           issue_pv(t, j);
+          if (j + 1 < nb[t]) {
+            // In issue order after PV_t(j): overwrites P_t(j) only once PV_t(j) has read it.
+            if (!k_next) {
+              if (!wait_item(2 * j + 2)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(t, j + 1);
+          } else {
+            tc_commit(&o_full[t]);
+          }
         }
         if (!ok) break;
-        release_item(v_item(j));
+        release_item(2 * j + 1);
+        if (k_next) release_item(2 * j + 2);
       }
       tc_commit(drain);
       mbar_wait(drain, 0, kSiteTeardown);
@@ -386,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb[t]; ++j) {
+      // S_t(j) complete -- and with it PV_t(j-1), issued before it.
       if (!mbar_wait(&s_full[t], j & 1, kSiteSoftS)) {
         ok = false;
         break;
@@ -395,10 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < kBlockN / 32; ++c) tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       tmem_wait_ld();
-      // S_t(j) is in registers: the MMA warp may overwrite S_t with block j+1 now.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[t]);
       const int n0 = j * kBlockN;
       // Tile-uniform: does any row of this tile see a masked key in block j?
       const bool masked_block = (n0 + kBlockN > p.N) || (p.causal && n0 + kBlockN - 1 > q0 + t * kTileM);
@@ -426,76 +411,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l *= alpha;
       // The two tiles take turns on the exp phase (tile 0 block j, tile 1 block j, tile 0
-      // block j+1, ...): the MUFU pipe runs one tile's exponentials at full rate while the
-      // other tile loads S, reduces its max and stores P.  Tile 0 block j waits for tile 1's
-      // block j-1, tile 1 block j for tile 0's block j (skipped where the other tile has no
-      // such block); each tile's turns complete in order, so parities stay one phase apart.
-      if (t == 0 ? (j >= 1 && j - 1 < nb[1]) : (j < nb[0])) {
+      // block j+1, ...): the MUFU pipe runs one tile's exponentials at full rate.  Tile 0
+      // block j waits for tile 1's block j-1, tile 1 block j for tile 0's block j (skipped
+      // where the other tile has no such block); each tile's turns complete in order, so
+      // parities stay one phase apart.
+      if (kExpTurns && (t == 0 ? (j >= 1 && j - 1 < nb[1]) : (j < nb[0]))) {
         if (!mbar_wait(&exp_tok[t], (t == 0 ? j - 1 : j) & 1, kSiteSoftS)) {
           ok = false;
           break;
         }
       }
       // p = 2^(s * scale * log2e - m_used), packed two per 32-bit word in the input dtype.
-      const float neg = -m_used;
-      float rs0 = 0.f, rs1 = 0.f;
+      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
+      const uint64_t ng2 = f2(-m_used, -m_used);
+      uint64_t rs2 = f2(0.f, 0.f);
       uint32_t pk[kBlockN / 2];
 #pragma unroll
       for (int e = 0; e < kBlockN / 2; ++e) {
+        const uint64_t x2 = fma2(f2(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])), sc2, ng2);
         float p0, p1;
         if (e % 16 < kPolyPairs && !masked_block) {
-          uf2(exp2_poly2(f2(fmaf(__uint_as_float(sr[2 * e]), p.scale_log2, neg),
-                            fmaf(__uint_as_float(sr[2 * e + 1]), p.scale_log2, neg))),
-              p0, p1);
+          uf2(exp2_poly2(x2), p0, p1);
         } else {
-          p0 = ex2(fmaf(__uint_as_float(sr[2 * e]), p.scale_log2, neg));
-          p1 = ex2(fmaf(__uint_as_float(sr[2 * e + 1]), p.scale_log2, neg));
+          float x0, x1;
+          uf2(x2, x0, x1);
+          p0 = ex2(x0);
+          p1 = ex2(x1);
         }
-        rs0 += p0;
-        rs1 += p1;
+        rs2 = add2(rs2, f2(p0, p1));
         pk[e] = pack2<kBf16>(p0, p1);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&exp_tok[1 - t]);  // the other tile's turn
-      l += rs0 + rs1;
-      if (j > 0) {
-        // PV_t(j-1) must be done before P_t is overwritten and O_t is rescaled.
-        if (!mbar_wait(&pv_done[t], (j - 1) & 1, kSiteSoftO)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (warp_rescale) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(o_tmem + c * 32, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st32(o_tmem + c * 32, ov);
-          }
-        }
+      if (kExpTurns) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&exp_tok[1 - t]);  // the other tile's turn
       }
-      // P_t row r -> smem in the K-major 128B-swizzled layout the PV MMA reads: two 64-key
-      // halves of 128 rows x 128 B; 16-byte chunk c of row r lands at chunk c ^ (r & 7).
       {
-        uint8_t* prow = sP + t * C::kPBytes + r * 128;
+        float rs0, rs1;
+        uf2(rs2, rs0, rs1);
+        l += rs0 + rs1;
+      }
+      // P_t(j) -> the first 64 columns of S_t (this thread's row, two keys per column).
+      tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(s_tmem + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+      if (warp_rescale) {
+        // O_t holds exactly PV_t(0..j-1) (complete): rescale it before PV_t(j) accumulates.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(o_tmem + c * 32, ov);
+          tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < kBlockN / 8; ++q) {
-          uint4 w = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(prow + (q >> 3) * (kTileM * 128) + ((((q & 7) ^ (r & 7))) << 4)) = w;
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(o_tmem + c * 32, ov);
         }
       }
-      fence_proxy_async_smem();  // generic-proxy P stores -> visible to the tensor core
-      if (warp_rescale) tmem_wait_st();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // Epilogue: O / l -> global.
     if (ok && nb[t] > 0) {
-      if (mbar_wait(&pv_done[t], (nb[t] - 1) & 1, kSiteSoftO)) {
+      if (mbar_wait(&o_full[t], 0, kSiteSoftO)) {
         tc_fence_after();
         const float inv = 1.f / l;
         const bool row_ok = m < p.M;

@@ -39,6 +39,12 @@ enum DeviceCode : int {
 #define LK_WAIT_LIMIT_NS 1000000000ull
 #endif
 
+// Spins between two checks of the wall clock and of the grid-wide failure flag in a bounded
+// wait (the flag is a global load, so it is not read on every spin).
+#ifndef LK_WAIT_CHECK_MASK
+#define LK_WAIT_CHECK_MASK 63u
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -71,7 +77,7 @@ __device__ __forceinline__ bool wait_counter_gt(const int* ctr, int value, int s
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (ld_acquire_gpu(ctr) <= value) {
-    if ((++spins & 63u) == 0) {
+    if ((++spins & LK_WAIT_CHECK_MASK) == 0) {
       if (device_failed()) return false;
       if (globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
         record_failure(kDevTimeout, site);
@@ -131,7 +137,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+    if ((++spins & LK_WAIT_CHECK_MASK) == 0) {
       if (device_failed()) return false;
       if (globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
         record_failure(kDevTimeout, site);
@@ -364,6 +370,14 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// The descriptor of (the descriptor's start address + off_bytes): only the 14-bit start field
+// (address >> 4) changes, and shared-memory addresses below 256 KB never carry out of it, so
+// one 32-bit add on the low word replaces rebuilding the descriptor in an MMA issue loop.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t off_bytes) {
+  const uint32_t lo = (uint32_t)desc + (off_bytes >> 4);
+  return (desc & 0xFFFFFFFF00000000ull) | lo;
+}
+
 // Instruction descriptor (dense, no negate, no saturate).
 //   c_fmt: 0 f16, 1 f32, 2 s32        (bits [4,6))
 //   a_fmt/b_fmt: kind::f16 -> 0 f16, 1 bf16; kind::tf32 -> 2; kind::i8 -> 1 signed  ([7,10),[10,13))
@@ -430,7 +444,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+    if ((++spins & LK_WAIT_CHECK_MASK) == 0) {
       if (device_failed()) return false;
       if (globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
         record_failure(kDevTimeout, site);
