@@ -171,7 +171,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 template <int D, bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                  const __grid_constant__ CUtensorMap tmV, const Params p) {
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Params p) {
   using C = Cfg<D>;
   constexpr int S = C::kStages;
   constexpr bool kExpTurns = exp_turns<D>();
@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
@@ -470,30 +471,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    // Epilogue: O / l -> global.
+    // Epilogue: O / l -> this warp's 32 rows of the tile's Q buffer (idle now: every MMA that
+    // reads Q_t is complete once o_full_t is), 128B-swizzled like a TMA tile, then TMA stores
+    // of 64-column x 32-row boxes; rows past M are clipped by the copy.  Row-per-thread global
+    // stores would touch 32 cache lines per instruction.
     if (ok && nb[t] > 0) {
       if (mbar_wait(&o_full[t], 0, kSiteSoftO)) {
         tc_fence_after();
         const float inv = 1.f / l;
-        const bool row_ok = m < p.M;
-        uint16_t* orow = static_cast<uint16_t*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)m * p.o_sm;
+        uint8_t* stage = sQ + t * C::kTileBytes + quad * (32 * 128);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ov[32];
           tmem_ld32(o_tmem + c * 32, ov);
           tmem_wait_ld();
-          if (row_ok) {
+          uint8_t* box_row = stage + (c >> 1) * (kTileM * 128) + lane * 128;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack2<kBf16>(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv);
-              w.y = pack2<kBf16>(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv);
-              w.z = pack2<kBf16>(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv);
-              w.w = pack2<kBf16>(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv);
-              reinterpret_cast<uint4*>(orow + c * 32)[q] = w;
-            }
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<kBf16>(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv);
+            w.y = pack2<kBf16>(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv);
+            w.z = pack2<kBf16>(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv);
+            w.w = pack2<kBf16>(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv);
+            const int piece = (c & 1) * 4 + q;  // 16-byte piece of the 128-byte box row
+            *reinterpret_cast<uint4*>(box_row + ((piece ^ (lane & 7)) << 4)) = w;
           }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int row0 = q0 + t * kTileM + quad * 32;
+        if (lane == 0 && row0 < p.M) {
+          for (int x = 0; x < C::kQBoxes; ++x) tma_store_4d(&tmO, stage + x * (kTileM * 128), 64 * x, row0, h, b);
+          bulk_commit_group();
+          bulk_wait_group<0>();  // the copy has read shared memory and written O
+        }
+        __syncwarp();
       }
     }
   }
@@ -505,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D, bool kBf16>
-int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const Params& p, cudaStream_t s) {
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to, const Params& p,
+           cudaStream_t s) {
   using C = Cfg<D>;
   auto kern = fa_fwd_kernel<D, kBf16>;
   static std::atomic<uint64_t> configured{0};
@@ -518,16 +531,16 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, 
     configured.fetch_or(bit);
   }
   const int64_t grid = (int64_t)p.num_qblocks * p.B * p.H;
-  kern<<<(unsigned)grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, p);
+  kern<<<(unsigned)grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, to, p);
   return check_launch();
 }
 
 int make_map(CUtensorMap* map, bool bf16, const void* base, int64_t B, int64_t H, int64_t S, int64_t D,
-             const int64_t* st) {
+             const int64_t* st, uint32_t box_rows = 128) {
   if (st[3] != 1) return LK_ERR_INVALID_ARG;
   const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
   const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
-  const uint32_t box[4] = {64, 128, 1, 1};
+  const uint32_t box[4] = {64, box_rows, 1, 1};
   return make_tmap(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims,
                    strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -559,6 +572,8 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   if (int st = fa::make_map(&tq, bf16, q, B, H, M, D, q_strides)) return st;
   if (int st = fa::make_map(&tk, bf16, k, B, H, N, D, k_strides)) return st;
   if (int st = fa::make_map(&tv, bf16, v, B, H, N, D, v_strides)) return st;
+  CUtensorMap to;  // O: 32-row boxes, one per softmax warp
+  if (int st = fa::make_map(&to, bf16, o, B, H, M, D, o_strides, 32)) return st;
   fa::Params p{};
   p.B = (int)B;
   p.H = (int)H;
@@ -577,6 +592,7 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   p.o_sb = o_strides[0];
   p.o_sh = o_strides[1];
   p.o_sm = o_strides[2];
-  if (D == 128) return bf16 ? fa::launch<128, true>(tq, tk, tv, p, s) : fa::launch<128, false>(tq, tk, tv, p, s);
-  return bf16 ? fa::launch<64, true>(tq, tk, tv, p, s) : fa::launch<64, false>(tq, tk, tv, p, s);
+  if (D == 128)
+    return bf16 ? fa::launch<128, true>(tq, tk, tv, to, p, s) : fa::launch<128, false>(tq, tk, tv, to, p, s);
+  return bf16 ? fa::launch<64, true>(tq, tk, tv, to, p, s) : fa::launch<64, false>(tq, tk, tv, to, p, s);
 }
