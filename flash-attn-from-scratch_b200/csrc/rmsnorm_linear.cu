@@ -18,9 +18,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstring>
 #include <mutex>
 
-#include "gemm_sm100.cuh"
+#include "gemm_pair_sm100.cuh"
 #include "lk_abi.h"
 
 namespace lk {
@@ -194,7 +195,48 @@ int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y
       static_cast<const T*>(x), x_ld, (int)rows, (int)d_in, eps, rstd);
   if (int st = check_launch()) return st;
 
-  // 2) the GEMM, a programmatic dependent of (1)
+  // 2) the GEMM, a programmatic dependent of (1).  With enough 256 x 256 tiles to occupy
+  //    every SM pair: the CTA-pair kernel (each CTA loads half of every W tile, C leaves
+  //    through TMA store tiles); otherwise the one-CTA kernel.
+#ifndef LK_RMS_PAIR
+#define LK_RMS_PAIR 1
+#endif
+  {
+    const int ptm = (int)((rows + 255) / 256), ptn = (int)((d_out + 255) / 256);
+    if (LK_RMS_PAIR && (int64_t)ptm * ptn >= num_sms / 2) {
+      CUtensorMap tbp, tc;
+      {
+        const uint64_t dims[2] = {(uint64_t)d_in, (uint64_t)d_out};
+        const uint64_t strides[1] = {(uint64_t)d_in * 2};
+        const uint32_t box[2] = {64, 128};
+        if (int st = make_tmap(&tbp, tdt, 2, w_fold, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+      }
+      gemm::Params p{};
+      p.M = (int)rows;
+      p.N = (int)d_out;
+      p.K = (int)d_in;
+      p.tiles_m = ptm;
+      p.tiles_n = ptn;
+      p.num_tiles = ptm * ptn;
+      p.C = y;
+      p.ldc = y_ld;
+      p.rstd = rstd;
+      p.full_tiles = p.num_tiles;
+      p.split = 1;
+      p.num_units = p.num_tiles;
+      memset(&tc, 0, sizeof(tc));
+      {
+        const uint64_t dims[2] = {(uint64_t)d_out, (uint64_t)rows};
+        const uint64_t strides[1] = {(uint64_t)y_ld * 2};
+        const uint32_t box[2] = {32, 32};
+        p.c_tma = (aligned16(y) && (y_ld * 2) % 16 == 0 &&
+                   make_tmap(&tc, tdt, 2, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B) == LK_OK)
+                      ? 1
+                      : 0;
+      }
+      return cuda_status((cudaError_t)gemm::launch_pair<kKind, false, Epi::RowRsqrt>(ta, tbp, tc, p, num_sms, s));
+    }
+  }
   gemm::Params p{};
   p.M = (int)rows;
   p.N = (int)d_out;
