@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = pair; u < p.num_units && ok; u += npairs) {
         const Unit w = decode_unit(u, p, num_kb);
         int mb, nb;
-        tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb, p.group_m);
         const int m0 = mb * kPairM + (int)rank * kBM;
         const int n0 = nb * Cfg::kBN + (int)rank * Cfg::kHalfN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = pair; u < p.num_units; u += npairs, ++local) {
       const Unit w = decode_unit(u, p, num_kb);
       int mb, nb;
-      tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb, p.group_m);
       const int m = mb * kPairM + (int)rank * kBM + row_in_tile;
       const int m_warp = m - lane;  // first row of this warp's 32
       const int n_base = nb * Cfg::kBN;

@@ -55,6 +55,7 @@ struct Params {
   int full_tiles, split, num_units;
   uint4* split_partial;  // [tail writers][8 warp slots][8 chunks][8][32] partial accumulators
   int c_tma;             // CTA-pair kernel: C is written by TMA stores through the tmC map
+  int group_m;           // CTA-pair kernel: M-blocks per raster group
   int* split_flags;      // [tail tiles x 8] arrival counters, then [tail writers x 8] chunk counters
 };
 
@@ -104,11 +105,13 @@ struct Config {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
-  const int per_group = kGroupM * tiles_n;
+// Tile raster: groups of `group_m` M-blocks sweep all N-blocks, so a group's A rows stay in
+// L2 while every B tile is read once per group.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb, int group_m = kGroupM) {
+  const int per_group = group_m * tiles_n;
   const int g = t / per_group;
-  const int first_m = g * kGroupM;
-  const int gsz = min(tiles_m - first_m, kGroupM);
+  const int first_m = g * group_m;
+  const int gsz = min(tiles_m - first_m, group_m);
   const int r = t - g * per_group;
   mb = first_m + r % gsz;
   nb = r / gsz;

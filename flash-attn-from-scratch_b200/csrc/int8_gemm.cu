@@ -147,6 +147,10 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
       p.sa = sa;
       p.sb = sb;
       p.rstd = nullptr;
+#ifndef LK_GEMM_PAIR_GROUP_M
+#define LK_GEMM_PAIR_GROUP_M 16
+#endif
+      p.group_m = LK_GEMM_PAIR_GROUP_M;
       p.full_tiles = p.num_tiles;
       p.split = 1;
       p.num_units = p.num_tiles;

@@ -221,6 +221,10 @@ int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y
       p.C = y;
       p.ldc = y_ld;
       p.rstd = rstd;
+#ifndef LK_GEMM_PAIR_GROUP_M
+#define LK_GEMM_PAIR_GROUP_M 16
+#endif
+      p.group_m = LK_GEMM_PAIR_GROUP_M;
       p.full_tiles = p.num_tiles;
       p.split = 1;
       p.num_units = p.num_tiles;
