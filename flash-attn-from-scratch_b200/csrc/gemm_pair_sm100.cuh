@@ -445,7 +445,8 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMa
     if (e != cudaSuccess) return (int)e;
     configured.fetch_or(bit);
   }
-  const int pairs = p.num_tiles < num_sms / 2 ? p.num_tiles : num_sms / 2;
+  // Every unit (tile or split part) of the first round gets its own pair.
+  const int pairs = p.num_units < num_sms / 2 ? p.num_units : num_sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);

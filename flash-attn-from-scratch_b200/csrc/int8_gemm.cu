@@ -6,81 +6,17 @@
 // on sm_100a: the int32 accumulator lives in tensor memory and is dequantised straight from
 // TMEM in the epilogue, so it never touches HBM.
 #include <cstring>
-#include <map>
-#include <mutex>
-#include <utility>
 
 #include "gemm_pair_sm100.cuh"
+#include "gemm_split.h"
 #include "lk_abi.h"
 
 namespace lk {
 namespace {
 
-#ifndef LK_GEMM_SPLIT
-#define LK_GEMM_SPLIT 1
-#endif
 #ifndef LK_GEMM_TMA_STORE
 #define LK_GEMM_TMA_STORE 1
 #endif
-
-// Workspace of the pair kernel's split tail, one per (device, stream): launches on one stream
-// never overlap, and each launch leaves its counters zero, so nothing is shared between
-// concurrent launches.  Sized for the most tail writers a launch can have (fewer than the
-// pairs): 256 KB of partials and 16 counters per pair.  Allocated on first use outside stream
-// capture; a launch captured before its stream has a workspace simply runs unsplit.
-struct SplitWorkspace {
-  uint4* partial = nullptr;
-  int* flags = nullptr;
-};
-
-bool split_workspace(cudaStream_t stream, int npairs, SplitWorkspace* out) {
-  static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, SplitWorkspace> table;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = table.find(key);
-  if (it != table.end()) {
-    *out = it->second;
-    return true;
-  }
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return false;
-  }
-  SplitWorkspace ws;
-  const size_t partial_bytes = (size_t)npairs * 8 * 8 * 256 * sizeof(uint4);
-  const size_t flag_bytes = (size_t)npairs * 16 * sizeof(int);
-  if (cudaMalloc(&ws.partial, partial_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  if (cudaMalloc(&ws.flags, flag_bytes) != cudaSuccess || cudaMemsetAsync(ws.flags, 0, flag_bytes, stream) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(ws.partial);
-    if (ws.flags) cudaFree(ws.flags);
-    return false;
-  }
-  table[key] = ws;
-  *out = ws;
-  return true;
-}
-
-// Splits the last round of a pair launch along K when it would leave pairs idle and the
-// saved K blocks outweigh the partial round trip.  Returns the number of parts (1 = none).
-int choose_split(int num_tiles, int npairs, int num_kb) {
-  if (!LK_GEMM_SPLIT || num_tiles <= npairs) return 1;
-  const int tail = num_tiles % npairs;
-  if (tail == 0) return 1;
-  int s = npairs / tail;
-  if (s > 4) s = 4;
-  // Each part must keep enough K blocks that halving the tail beats writing and re-reading
-  // 128 KB of partials per CTA.
-  while (s > 1 && num_kb < 8 * s) --s;
-  return s;
-}
 
 using gemm::Epi;
 using gemm::Kind;
@@ -151,19 +87,7 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
 #define LK_GEMM_PAIR_GROUP_M 16
 #endif
       p.group_m = LK_GEMM_PAIR_GROUP_M;
-      p.full_tiles = p.num_tiles;
-      p.split = 1;
-      p.num_units = p.num_tiles;
-      const int npairs = p.num_tiles < num_sms / 2 ? p.num_tiles : num_sms / 2;
-      const int split = choose_split(p.num_tiles, npairs, (int)((K + 127) / 128));
-      SplitWorkspace ws;
-      if (split > 1 && split_workspace(stream, num_sms / 2, &ws)) {
-        p.full_tiles = p.num_tiles - p.num_tiles % npairs;
-        p.split = split;
-        p.num_units = p.full_tiles + (p.num_tiles - p.full_tiles) * split;
-        p.split_partial = ws.partial;
-        p.split_flags = ws.flags;
-      }
+      apply_split(p, num_sms / 2, (int)((K + 127) / 128), 4, stream);
       // C through TMA stores of 32-row x 64-byte tiles when its base and row pitch allow it.
       CUtensorMap tc;
       memset(&tc, 0, sizeof(tc));

@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "gemm_pair_sm100.cuh"
+#include "gemm_split.h"
 #include "lk_abi.h"
 
 namespace lk {
@@ -202,7 +203,11 @@ int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y
 #define LK_RMS_PAIR 1
 #endif
   {
+    // (Fewer tiles than pairs, split along K, measured slower: such problems are bound by the
+    // TMA round trip, not by tensor or L2 throughput.)  Leftover tiles of the last round are
+    // split in at most 2 parts, so float partial sums do not depend on arrival order.
     const int ptm = (int)((rows + 255) / 256), ptn = (int)((d_out + 255) / 256);
+    const int num_kb = (int)((d_in + 63) / 64);
     if (LK_RMS_PAIR && (int64_t)ptm * ptn >= num_sms / 2) {
       CUtensorMap tbp, tc;
       {
@@ -225,9 +230,7 @@ int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y
 #define LK_GEMM_PAIR_GROUP_M 16
 #endif
       p.group_m = LK_GEMM_PAIR_GROUP_M;
-      p.full_tiles = p.num_tiles;
-      p.split = 1;
-      p.num_units = p.num_tiles;
+      gemm::apply_split(p, num_sms / 2, num_kb, 2, s);
       memset(&tc, 0, sizeof(tc));
       {
         const uint64_t dims[2] = {(uint64_t)d_out, (uint64_t)rows};
