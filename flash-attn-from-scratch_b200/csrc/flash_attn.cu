@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;       // [2]   P_t(j) in TMEM, O_t rescaled (4 warp arrivals)
   uint64_t* o_full = p_full + 2;       // [2]   last PV_t complete (tcgen05.commit)
   uint64_t* exp_tok = o_full + 2;      // [2]   exp_tok[t]: the other tile finished an exp phase
-  uint64_t* drain = exp_tok + 2;       // [1]
+  uint64_t* p_half = exp_tok + 2;      // [2]   keys 0-63 of P_t(j) in TMEM, O_t rescaled (4 warp arrivals)
+  uint64_t* drain = p_half + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = warp_id();
@@ -234,6 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
+      mbar_init(&p_half[t], 4);
       mbar_init(&o_full[t], 1);
       mbar_init(&exp_tok[t], 4);
     }
@@ -309,12 +311,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // O_t (+)= P_t V : A = P_t from TMEM (columns [128t, 128t+64), two keys per column),
       // B = V MN-major from shared memory.
-      auto issue_pv = [&](int t, int blk) {
+      // Issued in two key halves: keys 0-63 as soon as that half of P is in TMEM.
+      auto issue_pv = [&](int t, int blk, int ks0, int ks1) {
         const uint64_t vd = sdesc_add(ring_v_desc, ((2 * blk + 1) % S) * C::kTileBytes);
         const uint32_t o_tmem = tmem + C::kOCol0 + t * D;
         const uint32_t p_tmem = tmem + t * kBlockN;
 #pragma unroll
-        for (int ks = 0; ks < kBlockN / 16; ++ks)
+        for (int ks = ks0; ks < ks1; ++ks)
           mma_f16_ts(o_tmem, p_tmem + ks * 8, sdesc_add(vd, ks * 16 * 128), kIdescO, (blk > 0 || ks > 0) ? 1u : 0u);
       };
       // Prologue: S_t(0) for both tiles.
@@ -333,12 +336,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool k_next = false;  // K_{j+1} is in (and used by this iteration)
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= nb[t]) continue;
+          if (!mbar_wait(&p_half[t], j & 1, kSiteMmaP)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, j, 0, kBlockN / 32);
           if (!mbar_wait(&p_full[t], j & 1, kSiteMmaP)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(t, j);
+          issue_pv(t, j, kBlockN / 32, kBlockN / 16);
           if (j + 1 < nb[t]) {
             // In issue order after PV_t(j): overwrites P_t(j) only once PV_t(j) has read it.
             if (!k_next) {
@@ -441,6 +450,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         rs2 = add2(rs2, f2(p0, p1));
         pk[e] = pack2<kBf16>(p0, p1);
+        if (e == kBlockN / 4 - 1) {
+          // Keys 0-63 of P_t(j) -> columns 0-31 of S_t (this thread's row, two keys per column);
+          // the MMA warp starts PV_t(j) on them while the rest are computed.
+          tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+          if (warp_rescale) {
+            // O_t holds exactly PV_t(0..j-1) (complete since S_t(j) is): rescale it before the
+            // first half of PV_t(j) accumulates -- here, where half of S is no longer live.
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tmem_ld32(o_tmem + c * 32, ov);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+              tmem_st32(o_tmem + c * 32, ov);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_half[t]);
+        }
       }
       if (kExpTurns) {
         __syncwarp();
@@ -451,21 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uf2(rs2, rs0, rs1);
         l += rs0 + rs1;
       }
-      // P_t(j) -> the first 64 columns of S_t (this thread's row, two keys per column).
-      tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      // Keys 64-127 of P_t(j) -> columns 32-63 of S_t.
       tmem_st32(s_tmem + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
-      if (warp_rescale) {
-        // O_t holds exactly PV_t(0..j-1) (complete): rescale it before PV_t(j) accumulates.
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(o_tmem + c * 32, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st32(o_tmem + c * 32, ov);
-        }
-      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
