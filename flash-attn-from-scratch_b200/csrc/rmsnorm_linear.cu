@@ -166,9 +166,11 @@ int run_fold(const void* w_norm, int w_norm_dtype, const void* w_lin, void* w_fo
   return check_launch();
 }
 
+// may_allocate = false: nothing is allocated (the CTA-pair kernel's split workspace is not
+// used), for the no-allocation entry point.
 template <Kind kKind>
 int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld, int64_t rows, int64_t d_in,
-             int64_t d_out, float eps, float* rstd, cudaStream_t s) {
+             int64_t d_out, float eps, float* rstd, cudaStream_t s, bool may_allocate) {
   using T = typename std::conditional<kKind == Kind::F16, __half, __nv_bfloat16>::type;
   const CUtensorMapDataType tdt = kKind == Kind::F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int num_sms = sm_count();
@@ -230,7 +232,7 @@ int run_gemm(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y
 #define LK_GEMM_PAIR_GROUP_M 16
 #endif
       p.group_m = LK_GEMM_PAIR_GROUP_M;
-      gemm::apply_split(p, num_sms / 2, num_kb, 2, s);
+      gemm::apply_split(p, num_sms / 2, num_kb, may_allocate ? 2 : 1, s);
       memset(&tc, 0, sizeof(tc));
       {
         const uint64_t dims[2] = {(uint64_t)d_out, (uint64_t)rows};
@@ -279,10 +281,10 @@ extern "C" int lk_rmsnorm_linear_fold(const void* w_norm, int w_norm_dtype, cons
                          : run_fold<__nv_bfloat16>(w_norm, w_norm_dtype, w_lin, w_fold, d_in, d_out, s);
 }
 
-extern "C" int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld, int dtype,
-                                 int64_t rows, int64_t d_in, int64_t d_out, float eps, float* row_rstd,
-                                 void* stream) {
-  using namespace lk;
+namespace lk {
+namespace {
+int rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld, int dtype, int64_t rows,
+                   int64_t d_in, int64_t d_out, float eps, float* row_rstd, void* stream, bool may_allocate) {
   if (rows < 0 || d_in < 0 || d_out < 0) return LK_ERR_INVALID_ARG;
   if (rows == 0 || d_out == 0) return LK_OK;
   if (!x || !w_fold || !y || !row_rstd || d_in == 0) return LK_ERR_INVALID_ARG;
@@ -293,8 +295,17 @@ extern "C" int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (int st = bind_stream(s)) return st;
   return dtype == LK_F16
-             ? run_gemm<gemm::Kind::F16>(x, x_ld, w_fold, y, y_ld, rows, d_in, d_out, eps, row_rstd, s)
-             : run_gemm<gemm::Kind::BF16>(x, x_ld, w_fold, y, y_ld, rows, d_in, d_out, eps, row_rstd, s);
+             ? run_gemm<gemm::Kind::F16>(x, x_ld, w_fold, y, y_ld, rows, d_in, d_out, eps, row_rstd, s, may_allocate)
+             : run_gemm<gemm::Kind::BF16>(x, x_ld, w_fold, y, y_ld, rows, d_in, d_out, eps, row_rstd, s,
+                                          may_allocate);
+}
+}  // namespace
+}  // namespace lk
+
+extern "C" int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld, int dtype,
+                                 int64_t rows, int64_t d_in, int64_t d_out, float eps, float* row_rstd,
+                                 void* stream) {
+  return lk::rmsnorm_linear(x, x_ld, w_fold, y, y_ld, dtype, rows, d_in, d_out, eps, row_rstd, stream, true);
 }
 
 extern "C" int lk_fused_rmsnorm_linear(const void* X, const void* W_norm, const void* W_lin, void* Y, float eps,
@@ -346,5 +357,5 @@ extern "C" int lk_rmsnorm_linear_noalloc(const void* x, int64_t x_ld, const void
   if (int st = static_rstd_address(&rstd)) return st;
   // Every element of rstd[0, rows) is written by the row kernel before the GEMM reads it, so
   // whatever the previous call left in the array needs no clearing.
-  return lk_rmsnorm_linear(x, x_ld, w_fold, y, y_ld, dtype, rows, d_in, d_out, eps, rstd, stream);
+  return rmsnorm_linear(x, x_ld, w_fold, y, y_ld, dtype, rows, d_in, d_out, eps, rstd, stream, false);
 }

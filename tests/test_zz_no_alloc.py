@@ -74,3 +74,25 @@ def test_no_alloc_rejects_rows_beyond_the_fixed_scratch():
     st = lib.lk_rmsnorm_linear_noalloc(None, 64, None, None, 64, _lib.LK_BF16, 65537, 64, 64, 1e-6, None)
     assert st == _lib.LK_ERR_SCRATCH_LIMIT
     assert b"65536" in lib.lk_status_string(st)
+
+
+def test_no_alloc_allocates_nothing_on_the_pair_path():
+    """2304 x 1024 -> 2304 runs on the CTA-pair GEMM, whose split tail would take a per-stream
+    workspace on the entry point with caller scratch; the no-allocation entry point must leave
+    device memory untouched, on a stream it has never seen."""
+    _lib.set_device(0)
+    x, w_norm, w_lin = _inputs(2304, 1024, 2304, 3)
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        w_fold = _fold(w_norm, w_lin, side.cuda_stream)
+        y = torch.empty(2304, 2304, dtype=x.dtype, device=x.device)
+        y.zero_()  # the stream's first kernel: any lazy per-stream set-up happens here
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    _lib.call("lk_rmsnorm_linear_noalloc", x.data_ptr(), 1024, w_fold.data_ptr(), y.data_ptr(), 2304,
+              _lib.LK_BF16, 2304, 1024, 2304, 1e-6, side.cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    ref = _with_scratch(x, w_fold, 1e-6, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _rel(y, ref) <= REL_TOL
