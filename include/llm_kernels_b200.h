@@ -87,7 +87,12 @@ LK_API int lk_quantize_symmetric(const void* x, int x_dtype, int64_t rows, int64
  *     0 = [K,N] row-major, row stride ldb (the reference's layout, int8_gemm.py:100),
  *     1 = [N,K] row-major, row stride ldb (a weight's natural layout; no transpose copy).
  * C is fp16 [M,N] row-major with row stride ldc.
- * Requirements: K % 16 == 0; lda, ldb, ldc and the base pointers 16-byte aligned. */
+ * Requirements: K % 16 == 0; lda, ldb, ldc and the base pointers 16-byte aligned.
+ * Memory: when a problem's 256 x 256 tiles do not fill whole rounds of SM pairs, the leftover
+ * tiles are split along K through a workspace the library allocates once per (device, stream)
+ * on first need (~19 MB on a 148-SM part) and keeps; a call captured into a CUDA graph before
+ * its stream has one runs unsplit.  Calls on one stream share it (they never overlap); calls
+ * on different streams use different workspaces. */
 LK_API int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
                          const float* scale_a, const float* scale_b, void* C, int64_t ldc,
                          int64_t M, int64_t N, int64_t K, void* stream);
@@ -127,7 +132,9 @@ LK_API int lk_flash_attn_fwd(const void* q, const void* k, const void* v, void* 
  * programmatic dependent of the row kernel: only its epilogue waits for row_rstd.
  * dtype LK_F16 or LK_BF16 for x, w_fold and y.  x [rows, d_in] and y [rows, d_out] are
  * row-major with row strides x_ld, y_ld (elements); w_fold is [d_out, d_in] contiguous.
- * Requirements: d_in % 8 == 0, x_ld % 8 == 0, 16-byte aligned base pointers. */
+ * Requirements: d_in % 8 == 0, x_ld % 8 == 0, 16-byte aligned base pointers.
+ * Memory: large problems may take the same per-(device, stream) split workspace as the int8
+ * GEMM (see there); lk_rmsnorm_linear_noalloc never does. */
 LK_API int lk_rmsnorm_linear_fold(const void* w_norm, int w_norm_dtype, const void* w_lin, void* w_fold,
                                   int dtype, int64_t d_in, int64_t d_out, void* stream);
 LK_API int lk_rmsnorm_linear(const void* x, int64_t x_ld, const void* w_fold, void* y, int64_t y_ld,
