@@ -54,6 +54,9 @@ def fa_flops(b, h, n, d, causal):
     return 4.0 * b * h * n * n * d * (0.5 if causal else 1.0)
 
 
+SUSTAINED_AFTER_MS = 50.0  # timed regions at least this long are compared with the sustained peak
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -374,7 +377,14 @@ def run_ours(args):
             cpu = cpu_baselines()
 
     traffic = profile_traffic().get("flash_attn_causal_bf16_B4_H32_N4096_D128")
-    peak = float(peaks["bf16_tflops"])
+    # Denominator: the measured cuBLAS burst peak for a short timed region, the sustained one
+    # once the region is long enough for the power cap to engage (on this part FA throughput
+    # falls ~13% after ~45 ms of back-to-back launches); the burst fraction is reported too.
+    achieved = FLOPS_CAUSAL / (ms * 1e-3) / 1e12
+    burst = float(peaks["bf16_tflops"])
+    sustained = float(peaks.get("bf16_tflops_sustained", burst))
+    long_region = total_ms >= SUSTAINED_AFTER_MS
+    peak = sustained if long_region else burst
     line = {
         "metric": METRIC,
         "value": value,
@@ -391,11 +401,15 @@ def run_ours(args):
         "config": CONFIG,
         "roofline": {
             "bound": "tensor",
-            "achieved": FLOPS_CAUSAL / (ms * 1e-3) / 1e12,
+            "achieved": achieved,
             "peak": peak,
             "unit": "TFLOP/s",
-            "frac": FLOPS_CAUSAL / (ms * 1e-3) / 1e12 / peak,
-            "peak_kind": f"{peaks_kind} bf16 burst (cuBLAS), kernel timed alone",
+            "frac": achieved / peak,
+            "peak_kind": (f"{peaks_kind} bf16 sustained (cuBLAS, seconds-long loop under the power cap): the timed "
+                          f"region ({total_ms:.0f} ms of back-to-back launches) runs under the power cap"
+                          if long_region else
+                          f"{peaks_kind} bf16 burst (cuBLAS), kernel timed alone in a short region ({total_ms:.0f} ms)"),
+            "frac_of_burst": achieved / burst,
             "kernel": "lk::fa::fa_fwd_kernel<128, bf16>",
             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
             "algorithmic_bytes": 4 * nbytes,
