@@ -601,7 +601,7 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   {
     // causal: several waves per group, so heavy-first ordering still balances the tail
 #ifndef LK_FA_CAUSAL_WAVES
-#define LK_FA_CAUSAL_WAVES 4
+#define LK_FA_CAUSAL_WAVES 3
 #endif
     const int64_t g = LK_FA_GROUP_HEADS ? (causal ? LK_FA_CAUSAL_WAVES : 1) * sm_count() / nqb : B * H;
     p.group_heads = (int)(g < 1 ? 1 : (g > B * H ? B * H : g));
