@@ -478,6 +478,19 @@ def secondary_ops(args, llm_kernels, peaks):
     ms = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb), reps, 3, flush)
     ops["int8_gemm_dequant_4096_nk"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
                                         "layout": "B [N,K] (Int8Linear weight)"}
+    # The same GEMM with the raw int32 accumulator as output (like-for-like with the vendor line).
+    ms = time_each_flushed(lambda: llm_kernels.int8_gemm_i32(A_q, B_q, "nk"), reps, 3, flush)
+    ops["int8_gemm_i32_4096"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
+                                 "layout": "B [N,K], int32 output"}
+    # For comparison only (not part of the product): the vendor int8 GEMM (cuBLASLt through
+    # torch._int_mm, int32 output, no dequant) on the same operands, timed the same way.
+    try:
+        B_cm = B_q.t()  # [K, N] view of the [N, K] codes: column-major, as _int_mm wants
+        ms = time_each_flushed(lambda: torch._int_mm(A_q, B_cm), reps, 3, flush)
+        ops["vendor_int8_gemm_i32_4096"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
+                                            "what": "cuBLASLt int8 x int8 -> int32 via torch._int_mm (comparison)"}
+    except Exception as e:  # noqa: BLE001
+        ops["vendor_int8_gemm_i32_4096"] = {"unavailable": str(e)[:120]}
     # quantize_symmetric 4096x4096 fp16 (config 3b)
     ms = time_each_flushed(lambda: llm_kernels.quantize_symmetric(A_fp), reps, 3, flush)
     qbytes = 4096 * 4096 * 2 + 4096 * 4096 + 4096 * 4
