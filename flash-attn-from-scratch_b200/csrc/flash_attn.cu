@@ -42,13 +42,9 @@ constexpr int kThreads = 320;
 constexpr int kTileM = 128;   // query rows per tile
 constexpr int kBlockN = 128;  // keys per block
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-#ifndef LK_FA_POLY_PAIRS
-#define LK_FA_POLY_PAIRS 0
-#endif
 #ifndef LK_FA_GROUP_HEADS
 #define LK_FA_GROUP_HEADS 1  // 0: one global heavy-first order over all heads
 #endif
-constexpr int kPolyPairs = LK_FA_POLY_PAIRS;  // of every 16 exp2 pairs, this many on the FMA pipe
 // The two tiles take turns on the exp phase: measured faster at D = 128 (where the exp phase
 // is on each tile's critical chain), slower at D = 64.  -1 = per head dim, 0/1 = off/on.
 #ifndef LK_FA_EXP_TURNS
@@ -118,43 +114,10 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// 2^x for two lanes on the FMA/ALU pipes, relieving the MUFU pipe.  Cody-Waite split
-// x = r + f with r = round-to-nearest(x) (the 1.5*2^23 shifter leaves r in the low mantissa
-// bits) and f in [-0.5, 0.5]; 2^f from a cubic minimax polynomial fitted here by a Remez
-// exchange on relative error (max 7.5e-5 over [-0.5, 0.5]); 2^r added to the exponent
-// field.  x is clamped at -120 so the exponent never underflows.  Only used on key blocks
-// without masked (-inf) entries.
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
-  float x0, x1;
-  uf2(x, x0, x1);
-  x0 = fmaxf(x0, -120.f);
-  x1 = fmaxf(x1, -120.f);
-  const uint64_t xc = f2(x0, x1);
-  const uint64_t sh = f2(kShift, kShift);
-  const uint64_t t = add2(xc, sh);
-  const uint64_t f = sub2(xc, sub2(t, sh));
-  uint64_t p = fma2(f2(c3, c3), f, f2(c2, c2));
-  p = fma2(p, f, f2(c1, c1));
-  p = fma2(p, f, f2(c0, c0));
-  float t0, t1, p0, p1;
-  uf2(t, t0, t1);
-  uf2(p, p0, p1);
-  const float y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  const float y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-  return f2(y0, y1);
 }
 
 template <bool kBf16>
@@ -439,15 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < kBlockN / 2; ++e) {
         const uint64_t x2 = fma2(f2(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])), sc2, ng2);
-        float p0, p1;
-        if (e % 16 < kPolyPairs && !masked_block) {
-          uf2(exp2_poly2(x2), p0, p1);
-        } else {
-          float x0, x1;
-          uf2(x2, x0, x1);
-          p0 = ex2(x0);
-          p1 = ex2(x1);
-        }
+        float x0, x1;
+        uf2(x2, x0, x1);
+        const float p0 = ex2(x0);
+        const float p1 = ex2(x1);
         rs2 = add2(rs2, f2(p0, p1));
         pk[e] = pack2<kBf16>(p0, p1);
         if (e == kBlockN / 4 - 1) {
