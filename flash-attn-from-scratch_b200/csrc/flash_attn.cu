@@ -120,6 +120,24 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// Max of n fp32 values (bit patterns): four chains of three-input max over sr[4 .. n-4), the
+// first and last four values opening and closing the chains.
+template <int n>
+__device__ __forceinline__ float row_max(const uint32_t (&sr)[n]) {
+  static_assert(n % 8 == 0, "row length");
+  float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
+#pragma unroll
+  for (int c = 4; c < n - 4; c += 8) {
+    mx4[0] = max3(mx4[0], __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+    mx4[1] = max3(mx4[1], __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+    mx4[2] = max3(mx4[2], __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+    mx4[3] = max3(mx4[3], __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+  }
+  mx4[0] = max3(mx4[0], __uint_as_float(sr[n - 4]), __uint_as_float(sr[n - 3]));
+  mx4[1] = max3(mx4[1], __uint_as_float(sr[n - 2]), __uint_as_float(sr[n - 1]));
+  return fmaxf(max3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+}
+
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (kBf16) {
@@ -354,26 +372,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       uint32_t sr[kBlockN];
-#pragma unroll
-      for (int c = 0; c < kBlockN / 32; ++c) tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tmem_wait_ld();
       const int n0 = j * kBlockN;
       // Tile-uniform: does any row of this tile see a masked key in block j?
       const bool masked_block = (n0 + kBlockN > p.N) || (p.causal && n0 + kBlockN - 1 > q0 + t * kTileM);
+#pragma unroll
+      for (int c = 0; c < kBlockN / 32; ++c) tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_wait_ld();
       if (masked_block && n0 + kBlockN - 1 > lim) {
 #pragma unroll
         for (int c = 0; c < kBlockN; ++c)
           if (n0 + c > lim) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
-#pragma unroll
-      for (int c = 4; c < kBlockN; c += 8) {
-        mx4[0] = max3(mx4[0], __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
-        mx4[1] = max3(mx4[1], __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-        mx4[2] = max3(mx4[2], __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-        mx4[3] = max3(mx4[3], __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-      }
-      const float mx = fmaxf(max3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+      const float mx = row_max<kBlockN>(sr);
       const float m_new = mx * p.scale_log2;
       const bool need = m_new > m_used + kRescaleThreshold;
       const bool warp_rescale = __any_sync(0xffffffffu, need) && j > 0;

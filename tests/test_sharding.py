@@ -33,9 +33,12 @@ def _init(rank, world, port, timeout_s=30):
             sys.path.insert(0, p)
     import torch.distributed as dist
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    # The rendezvous gets its own generous limit (spawned ranks may take a while to import
+    # torch on a loaded machine); timeout_s bounds the collectives only.
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group(
+        "gloo", store=store, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s)
+    )
     return dist
 
 
