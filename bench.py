@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--quick]
 
-Headline workload (the metric's first clause, configs[1] of the op set's benchmark list):
+Headline workload (the metric's first clause):
 flash-attention forward, causal, bf16, B=4 H=32 N=4096 D=128, TFLOP/s with causal FLOPs
 counted as half of dense (4*B*H*N^2*D / 2).  One step = one flash_attn_forward call over
 one batch.  Inputs are 384 MiB per step (larger than the 126 MB L2), so no L2 flush is
@@ -515,7 +515,12 @@ def secondary_ops(args, llm_kernels, peaks):
     ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, k, v, causal=False), reps, 2, 1) / reps
     ops["flash_attn_noncausal_bf16_B4H32N4096D128"] = {"value": fa_flops(B, H, N, D, False) / (ms * 1e-3) / 1e12,
                                                        "unit": "TFLOP/s", "ms": ms}
-    del q, k, v
+    # grouped-query attention: 8 K/V heads shared by 32 query heads, read in place
+    kg, vg = k[:, :8].contiguous(), v[:, :8].contiguous()
+    ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, kg, vg, causal=True), reps, 2, 1) / reps
+    ops["flash_attn_gqa_causal_bf16_B4H32KV8N4096D128"] = {"value": fa_flops(B, H, N, D, True) / (ms * 1e-3) / 1e12,
+                                                           "unit": "TFLOP/s", "ms": ms}
+    del q, k, v, kg, vg
     # config 4 sweep: fp16, B8 H16 D64
     sweep = {}
     for n in ([512, 4096] if args.quick else [512, 1024, 2048, 4096, 8192, 16384]):

@@ -69,6 +69,7 @@ enum Site : int {
 struct Params {
   int B, H, M, N;
   int num_qblocks;  // ceil(M / 256)
+  int kv_group;     // query heads per K/V head (grouped-query attention; 1 = one K/V head each)
   int group_heads;  // heads per scheduling group (>= 1)
   int causal;
   float scale_log2;  // softmax scale * log2(e)
@@ -190,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int qb = p.num_qblocks - 1 - rem / gsz;
   const int bh = gbase + rem % gsz;
   const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / p.kv_group;  // K/V head of query head h
   const int q0 = qb * 2 * kTileM;
   const int nkb = (p.N + kBlockN - 1) / kBlockN;
   int nb[2];
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         const int row = (i >> 1) * kBlockN;
         uint8_t* dst = sRing + slot * C::kTileBytes;
-        for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, h, b);
+        for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, hk, b);
         issued = i + 1;
       }
       // Teardown: every copy issued must land before the CTA can exit.
@@ -538,8 +540,17 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
                                  int64_t H, int64_t M, int64_t N, int64_t D, const int64_t* q_strides,
                                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
                                  int causal, float softmax_scale, void* stream) {
+  return lk_flash_attn_fwd_gqa(q, k, v, o, dtype, B, H, H, M, N, D, q_strides, k_strides, v_strides, o_strides,
+                               causal, softmax_scale, stream);
+}
+
+extern "C" int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, int dtype, int64_t B,
+                                     int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
+                                     const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                     const int64_t* o_strides, int causal, float softmax_scale, void* stream) {
   using namespace lk;
   if (B < 0 || H < 0 || M < 0 || N < 0) return LK_ERR_INVALID_ARG;
+  if (H > 0 && (H_kv <= 0 || H % H_kv != 0)) return LK_ERR_INVALID_ARG;
   if (B == 0 || H == 0 || M == 0) return LK_OK;
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides || N == 0)
     return LK_ERR_INVALID_ARG;
@@ -556,8 +567,8 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   const bool bf16 = dtype == LK_BF16;
   CUtensorMap tq, tk, tv;
   if (int st = fa::make_map(&tq, bf16, q, B, H, M, D, q_strides)) return st;
-  if (int st = fa::make_map(&tk, bf16, k, B, H, N, D, k_strides)) return st;
-  if (int st = fa::make_map(&tv, bf16, v, B, H, N, D, v_strides)) return st;
+  if (int st = fa::make_map(&tk, bf16, k, B, H_kv, N, D, k_strides)) return st;
+  if (int st = fa::make_map(&tv, bf16, v, B, H_kv, N, D, v_strides)) return st;
   CUtensorMap to;  // O: 32-row boxes, one per softmax warp
   if (int st = fa::make_map(&to, bf16, o, B, H, M, D, o_strides, 32)) return st;
   fa::Params p{};
@@ -566,6 +577,7 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
   p.M = (int)M;
   p.N = (int)N;
   p.num_qblocks = (int)nqb;
+  p.kv_group = (int)(H / H_kv);
   {
     // causal: several waves per group, so heavy-first ordering still balances the tail
 #ifndef LK_FA_CAUSAL_WAVES

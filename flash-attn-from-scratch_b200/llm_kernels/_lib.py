@@ -46,6 +46,10 @@ SIGNATURES = {
         _i,
         [_p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64, _i, _f, _p],
     ),
+    "lk_flash_attn_fwd_gqa": (
+        _i,
+        [_p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64, _i, _f, _p],
+    ),
     "lk_rmsnorm_linear_fold": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _p]),
     "lk_rmsnorm_linear": (_i, [_p, _i64, _p, _p, _i64, _i, _i64, _i64, _i64, _f, _p, _p]),
     "lk_fused_rmsnorm_linear": (_i, [_p, _p, _p, _p, _f, _i64, _i64, _i64, _i, _p, _p, _p]),

@@ -3,7 +3,9 @@
 Drop-in for the reference's ``kernels/flash_attn/flash_attn_fwd.py:131-156``
 (``flash_attn_forward``), which dispatched to a non-causal (:6-64) or causal (:67-128) Triton
 kernel.  Same arguments and defaults; as a superset it also accepts bf16, ragged M/N (no
-tile-multiple requirement) and an optional ``softmax_scale``.
+tile-multiple requirement), an optional ``softmax_scale``, and K/V with fewer heads than Q
+(grouped-query / multi-query attention, the reference's ``experiments/attention_ablation.py``
+GroupedQueryAttention and MultiQueryAttention) read in place without repeating them.
 """
 
 from __future__ import annotations
@@ -21,7 +23,10 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
 
     Args:
         q : [B, H, M, D] fp16 / bf16, CUDA (any strides with a contiguous last dim)
-        k, v : [B, H, N, D], same dtype and device
+        k, v : [B, H_kv, N, D], same dtype and device; H_kv divides H and query head h
+            attends to K/V head h // (H // H_kv) (``repeat_interleave`` order,
+            attention_ablation.py:125-127).  H_kv = H is ordinary attention; a single K/V
+            head ``expand``-ed to H heads (attention_ablation.py:87-88) is read in place.
         causal : mask keys n > m (top-left aligned, flash_attn_fwd.py:118)
         block_m, block_n : accepted for signature compatibility; the sm_100a kernel uses
             its own 128-row tiles and handles any M, N.
@@ -42,7 +47,11 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
         require(isinstance(val, int) and val > 0, f"{name} must be a positive int")
     B, H, M, D = q.shape
     N = k.shape[2]
-    require(k.shape == (B, H, N, D) and v.shape == (B, H, N, D), "k and v must be [B, H, N, D] matching q")
+    if H > 1 and k.shape == (B, H, N, D) and v.shape == k.shape and k.stride(1) == 0 and v.stride(1) == 0:
+        k, v = k[:, :1], v[:, :1]  # one K/V head broadcast over the query heads
+    H_kv = k.shape[1]
+    require(H_kv > 0 and H % H_kv == 0 and k.shape == (B, H_kv, N, D) and v.shape == (B, H_kv, N, D),
+            "k and v must be [B, H_kv, N, D] matching q, with H_kv dividing H")
     require(0 < D <= 128, f"head dim {D} not supported (1..128)")
     scale = float(softmax_scale) if softmax_scale is not None else float(D) ** -0.5
     if out is not None:
@@ -78,10 +87,11 @@ def flash_attn_forward(q, k, v, causal=True, block_m=64, block_n=64, softmax_sca
         return out
     require(N > 0, "flash_attn_forward: need at least one key")
     s = stream_for(dev)
+    heads = (H,) if H_kv == H else (H, H_kv)
     _lib.call(
-        "lk_flash_attn_fwd",
+        "lk_flash_attn_fwd" if H_kv == H else "lk_flash_attn_fwd_gqa",
         ptr(q), ptr(k), ptr(v), ptr(out), dtype_code(q.dtype),
-        B, H, M, N, D,
+        B, *heads, M, N, D,
         _lib.i64_array(q.stride()), _lib.i64_array(k.stride()),
         _lib.i64_array(v.stride()), _lib.i64_array(out.stride()),
         1 if causal else 0, scale, s,

@@ -117,6 +117,18 @@ LK_API int lk_flash_attn_fwd(const void* q, const void* k, const void* v, void* 
                       const int64_t* v_strides, const int64_t* o_strides,
                       int causal, float softmax_scale, void* stream);
 
+/* Grouped-query / multi-query attention: K and V hold H_kv heads (H % H_kv == 0) and query
+ * head h attends to K/V head h / (H / H_kv) -- the reference's GroupedQueryAttention
+ * (experiments/attention_ablation.py:107-141, K/V heads repeat_interleave'd at :125-127) and,
+ * with H_kv = 1, MultiQueryAttention (:70-104, one K/V head expanded at :87-88), without
+ * materialising the repeated K/V.  k_strides/v_strides index the H_kv-head tensors; all else
+ * as lk_flash_attn_fwd, which is this call with H_kv = H. */
+LK_API int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, int dtype,
+                          int64_t B, int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
+                          const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, const int64_t* o_strides,
+                          int causal, float softmax_scale, void* stream);
+
 /* ---- fused RMSNorm + Linear --------------------------------------------------------------- *
  * Replaces csrc/fused_rmsnorm_linear.cu:105-120 (launch_fused_rmsnorm_linear) behind
  * csrc/bindings.cpp:26-67, and the fallback kernels/fused_rmsnorm_linear/fused_ops.py:27-37:

@@ -5,7 +5,7 @@ Restates the reference's fallback kernels/fused_rmsnorm_linear/fused_ops.py:27-3
     x_f = x.float(); rms = x_f.pow(2).mean(-1, keepdim=True).add(eps).rsqrt()
     x_norm = (x_f * rms * w_norm.float()).to(x.dtype); y = F.linear(x_norm, w_lin)
 Here every step stays in fp32 (``out_dtype`` selects a final rounding), which is the
-"repo's fp32 PyTorch RMSNorm+Linear path" the north star's tolerance is stated against.
+fp32 PyTorch RMSNorm+Linear path that the relative-error tolerance of 1e-2 is stated against.
 """
 
 from __future__ import annotations

@@ -2,7 +2,9 @@
 
 Run in a container that has the reference checkout (read-only) at /root/reference:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference] [op ...]
+
+(op: quantize, int8_gemm, flash_attn, rmsnorm_linear, gqa; default all)
 
 What it runs (all on the CPU):
   * ``quantize_symmetric``     kernels/int8_gemm/int8_gemm.py:146-161 (pure torch)
@@ -11,6 +13,9 @@ What it runs (all on the CPU):
   * ``flash_attn_fwd_kernel`` / ``flash_attn_fwd_causal_kernel``
     kernels/flash_attn/flash_attn_fwd.py:6-128 (Triton, interpreted)
   * ``_rmsnorm_linear_ref``    kernels/fused_rmsnorm_linear/fused_ops.py:27-37 (pure torch)
+  * ``GroupedQueryAttention`` / ``MultiQueryAttention``
+    experiments/attention_ablation.py:70-141 (torch modules; dropout 0, eval mode, the
+    output projection set to the identity so the module returns the attention output)
 Outputs: one ``.npz`` per op.  The fixtures are small (tens of KB) and committed; the GPU
 tests and the oracle tests read only the ``.npz`` files, never the reference.
 """
@@ -117,13 +122,41 @@ def make_rmsnorm_linear(ref):
     np.savez_compressed(os.path.join(HERE, "rmsnorm_linear.npz"), **out)
 
 
+def make_gqa(ref):
+    from experiments.attention_ablation import GroupedQueryAttention, MultiQueryAttention
+
+    out = {}
+    g = torch.Generator().manual_seed(15)
+    B, T, C, H = 1, 64, 128, 8  # head dim 16
+    D = C // H
+    for tag, mod in (("gqa", GroupedQueryAttention(C, H, n_kv_heads=2, dropout=0.0)),
+                     ("mqa", MultiQueryAttention(C, H, dropout=0.0))):
+        mod.eval()
+        with torch.no_grad():
+            for p in mod.parameters():
+                p.copy_(torch.randn(p.shape, generator=g) / C ** 0.5)
+            mod.out_proj.weight.copy_(torch.eye(C))
+            x = torch.randn(B, T, C, generator=g)
+            kh = mod.k_proj.out_features // D
+            out[f"{tag}_q"] = mod.q_proj(x).view(B, T, H, D).transpose(1, 2).contiguous().numpy()
+            out[f"{tag}_k"] = mod.k_proj(x).view(B, T, kh, D).transpose(1, 2).contiguous().numpy()
+            out[f"{tag}_v"] = mod.v_proj(x).view(B, T, kh, D).transpose(1, 2).contiguous().numpy()
+            for causal in (0, 1):
+                mask = torch.tril(torch.ones(T, T)) if causal else None
+                y = mod(x, mask)  # [B, T, C] = attention output with heads concatenated
+                out[f"{tag}_out_causal{causal}"] = y.view(B, T, H, D).transpose(1, 2).contiguous().numpy()
+    np.savez_compressed(os.path.join(HERE, "gqa.npz"), **out)
+
+
+MAKERS = {"quantize": make_quantize, "int8_gemm": make_int8_gemm, "flash_attn": make_flash_attn,
+          "rmsnorm_linear": make_rmsnorm_linear, "gqa": make_gqa}
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref)
-    make_quantize(ref)
-    make_int8_gemm(ref)
-    make_flash_attn(ref)
-    make_rmsnorm_linear(ref)
+    for name in sys.argv[2:] or list(MAKERS):
+        MAKERS[name](ref)
     print("golden vectors written to", HERE)
 
 

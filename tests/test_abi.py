@@ -55,6 +55,10 @@ def test_bad_arguments_rejected_on_host():
                                  null) == _lib.LK_ERR_INVALID_ARG
     assert lib.lk_rmsnorm_linear(null, 64, null, null, 64, _lib.LK_BF16, 4, 64, 64, 1e-6, null,
                                  null) == _lib.LK_ERR_INVALID_ARG
+    # grouped-query: H_kv must divide H (checked before any pointer or device use)
+    for h_kv in (0, -2, 3, 5):
+        assert lib.lk_flash_attn_fwd_gqa(null, null, null, null, _lib.LK_BF16, 1, 8, h_kv, 16, 16, 128, s4, s4, s4, s4,
+                                         1, 0.0, null) == _lib.LK_ERR_INVALID_ARG
 
 
 def test_empty_work_is_a_noop():

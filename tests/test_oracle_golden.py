@@ -65,6 +65,29 @@ def test_attention_fp32_vs_reference_kernel(causal):
     assert (out - ref).abs().max().item() < 1e-2
 
 
+@pytest.mark.parametrize("tag", ["gqa", "mqa"])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_attention_gqa_vs_reference_modules(tag, causal):
+    """The grouped-query oracle against the reference's GroupedQueryAttention (2 K/V heads for
+    8 query heads) and MultiQueryAttention modules run here in fp32."""
+    g = _load("gqa")
+    q, k, v = (torch.from_numpy(g[f"{tag}_{n}"]) for n in ("q", "k", "v"))
+    assert k.shape[1] == (2 if tag == "gqa" else 1) and q.shape[1] == 8
+    ref = torch.from_numpy(g[f"{tag}_out_causal{causal}"])
+    out = oracle.attention_gqa_fp32(q, k, v, causal=bool(causal))
+    assert (out - ref).abs().max().item() < 1e-5
+
+
+def test_attention_gqa_head_mapping_is_repeat_interleave():
+    """Query head h reads K/V head h // (H // H_kv), not h % H_kv: a planted modulo mapping
+    must disagree with the golden outputs."""
+    g = _load("gqa")
+    q, k, v = (torch.from_numpy(g[f"gqa_{n}"]) for n in ("q", "k", "v"))
+    ref = torch.from_numpy(g["gqa_out_causal0"])
+    wrong = oracle.attention_fp32(q, k.repeat(1, 4, 1, 1), v.repeat(1, 4, 1, 1), causal=False)
+    assert (wrong - ref).abs().max().item() > 1e-2
+
+
 @pytest.mark.parametrize("tag", ["f32", "f16"])
 def test_rmsnorm_linear_vs_reference(tag):
     g = _load("rmsnorm_linear")

@@ -1,7 +1,7 @@
 """Fused RMSNorm + Linear on the GPU vs the fp32 oracle (the reference's PyTorch path,
 kernels/fused_rmsnorm_linear/fused_ops.py:27-37).
 
-Tolerance (the north star's): relative error <= 1e-2, measured as
+Tolerance: relative error <= 1e-2, measured as
 max|y - y_ref| / max|y_ref| over the whole output.
 """
 
