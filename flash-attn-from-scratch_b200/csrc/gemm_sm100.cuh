@@ -57,7 +57,14 @@ struct Params {
   int c_tma;             // CTA-pair kernel: C is written by TMA stores through the tmC map
   int group_m;           // CTA-pair kernel: M-blocks per raster group
   int* split_flags;      // [tail tiles x 8] arrival counters, then [tail writers x 8] chunk counters
+  // Scatter epilogue (DequantF16 only): num_dst > 0 writes every output element to each of
+  // c_dst[0 .. num_dst) (each already offset to this GEMM's column block, row pitch ldc)
+  // instead of C -- e.g. the replicated outputs of all ranks of a column-sharded layer, peers'
+  // buffers mapped into this process over NVLink.
+  void* c_dst[8];
+  int num_dst;
 };
+constexpr int kMaxScatter = 8;
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle atom of K per stage
@@ -183,7 +190,7 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_s
   const bool full_chunk = (n0 + 32 <= p.N);
   if constexpr (kEpi == Epi::RawI32) {
     int32_t* crow = static_cast<int32_t*>(p.C) + (int64_t)m * p.ldc + n0;
-    if (full_chunk && (p.ldc % 4 == 0)) {
+    if (full_chunk && (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         reinterpret_cast<uint4*>(crow)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
@@ -196,9 +203,34 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_s
     float v[32];
     chunk_values<kKind, kEpi>(r, row_scale, n0, p, sbp,
                               full_chunk && ((reinterpret_cast<uintptr_t>(sbp) & 15) == 0), v);
-    uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
     constexpr bool kBf16Out = (kEpi == Epi::RowRsqrt && kKind == Kind::BF16);
-    if (full_chunk && (p.ldc % 8 == 0)) {
+    if constexpr (kEpi == Epi::DequantF16) {
+      if (p.num_dst > 0) {
+        // Scatter: the chunk is packed once and stored to every destination (16-byte stores
+        // where the pitch and every base allow them; the host checks both).
+        uint4 w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          w[j] = make_uint4(pack_out2<kKind, kEpi>(v[8 * j], v[8 * j + 1]), pack_out2<kKind, kEpi>(v[8 * j + 2], v[8 * j + 3]),
+                            pack_out2<kKind, kEpi>(v[8 * j + 4], v[8 * j + 5]),
+                            pack_out2<kKind, kEpi>(v[8 * j + 6], v[8 * j + 7]));
+#pragma unroll
+        for (int d = 0; d < kMaxScatter; ++d) {
+          if (d >= p.num_dst) break;
+          uint16_t* drow = static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)m * p.ldc + n0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(drow)[j] = w[j];
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) drow[j] = __half_as_ushort(__float2half_rn(v[j]));
+          }
+        }
+        return;
+      }
+    }
+    uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
+    if (full_chunk && (p.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         reinterpret_cast<uint4*>(crow)[j] =

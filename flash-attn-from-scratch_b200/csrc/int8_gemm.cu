@@ -45,9 +45,12 @@ int make_int8_maps(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, b
   }
 }
 
+// num_dst > 0 (DequantF16 only): no C; each output element goes to dsts[0 .. num_dst), device
+// pointers already offset to this GEMM's column block, all with row pitch ldc.
 template <Epi kEpi>
 int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout, const float* sa,
-             const float* sb, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+             const float* sb, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, cudaStream_t stream,
+             void* const* dsts = nullptr, int num_dst = 0) {
   if (M < 0 || N < 0 || K < 0) return LK_ERR_INVALID_ARG;
   if (b_layout != 0 && b_layout != 1) return LK_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return LK_OK;
@@ -59,7 +62,14 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   if (lda < K || ldc < N) return LK_ERR_INVALID_ARG;
   if (b_mn ? (ldb < N) : (ldb < K)) return LK_ERR_INVALID_ARG;
   if (lda % 16 || ldb % 16) return LK_ERR_ALIGNMENT;
+  if (num_dst > 0 && (ldc % 8 || kEpi != Epi::DequantF16)) return LK_ERR_ALIGNMENT;
+  for (int d = 0; d < num_dst; ++d)
+    if (!aligned16(dsts[d])) return LK_ERR_ALIGNMENT;
   if (int st = bind_stream(stream)) return st;
+  auto set_scatter = [&](gemm::Params& p) {
+    p.num_dst = num_dst;
+    for (int d = 0; d < num_dst; ++d) p.c_dst[d] = dsts[d];
+  };
 
   const int num_sms = sm_count();
 #ifndef LK_GEMM_PAIR
@@ -103,6 +113,10 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
                       ? 1
                       : 0;
       }
+      if (num_dst > 0) {
+        set_scatter(p);
+        p.c_tma = 0;  // the scatter stores from registers, to every destination
+      }
       const int err = b_mn ? gemm::launch_pair<Kind::I8, true, kEpi>(ta, tb, tc, p, num_sms, stream)
                            : gemm::launch_pair<Kind::I8, false, kEpi>(ta, tb, tc, p, num_sms, stream);
       return cuda_status((cudaError_t)err);
@@ -130,6 +144,7 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   p.sa = sa;
   p.sb = sb;
   p.rstd = nullptr;
+  set_scatter(p);
 
   int err;
   if (BN == 256) {
@@ -156,4 +171,19 @@ extern "C" int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, i
                                 int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream) {
   return lk::run_int8<lk::gemm::Epi::RawI32>(A, lda, B, ldb, b_layout, nullptr, nullptr, C, ldc, M, N, K,
                                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                                            int b_layout, const float* scale_a, const float* scale_b,
+                                            void* const* dsts, int num_dst, int64_t ldc, int64_t col_offset,
+                                            int64_t M, int64_t N, int64_t K, void* stream) {
+  if (num_dst < 1 || num_dst > lk::gemm::kMaxScatter || !dsts || col_offset < 0) return LK_ERR_INVALID_ARG;
+  if (N > 0 && ldc < col_offset + N) return LK_ERR_INVALID_ARG;
+  void* at[lk::gemm::kMaxScatter];
+  for (int d = 0; d < num_dst; ++d) {
+    if (!dsts[d]) return LK_ERR_INVALID_ARG;
+    at[d] = static_cast<uint16_t*>(dsts[d]) + col_offset;
+  }
+  return lk::run_int8<lk::gemm::Epi::DequantF16>(A, lda, B, ldb, b_layout, scale_a, scale_b, at[0], ldc, M, N, K,
+                                                 static_cast<cudaStream_t>(stream), at, num_dst);
 }

@@ -22,6 +22,7 @@ LK_ERR_CUDA = 3
 LK_ERR_TIMEOUT = 4
 LK_ERR_ALIGNMENT = 5
 LK_ERR_SCRATCH_LIMIT = 6
+LK_PEER_HANDLE_BYTES = 64  # include/llm_kernels_b200.h
 
 LK_F32, LK_F16, LK_BF16, LK_I8, LK_I32 = 0, 1, 2, 3, 4
 
@@ -42,6 +43,12 @@ SIGNATURES = {
     "lk_quantize_symmetric": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "lk_int8_gemm_dequant": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "lk_int8_gemm_i32": (_i, [_p, _i64, _p, _i64, _i, _p, _i64, _i64, _i64, _i64, _p]),
+    "lk_int8_gemm_dequant_scatter": (
+        _i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _p],
+    ),
+    "lk_peer_export": (_i, [_i, _p, _p, _pi64]),
+    "lk_peer_open": (_i, [_i, _p, _i64, ctypes.POINTER(ctypes.c_void_p)]),
+    "lk_peer_close": (_i, [_i, _p, _i64]),
     "lk_flash_attn_fwd": (
         _i,
         [_p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64, _i, _f, _p],

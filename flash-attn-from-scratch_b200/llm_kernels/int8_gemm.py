@@ -22,6 +22,7 @@ __all__ = [
     "int8_gemm_dequant_auto",
     "int8_gemm_i32",
     "int8_gemm_dequant_nk",
+    "int8_gemm_dequant_scatter",
 ]
 
 
@@ -133,6 +134,32 @@ def int8_gemm_dequant_nk(A, B_nk, scale_a, scale_b) -> torch.Tensor:
     """Same GEMM with B stored as [N, K] (a weight's natural layout), so no transpose copy."""
     M, N, K = _gemm_checks(A, B_nk, kn_layout=False)
     return _run_gemm(A, B_nk, 1, scale_a, scale_b, M, N, K, torch.float16)
+
+
+def int8_gemm_dequant_scatter(A, B_nk, scale_a, scale_b, dst_ptrs, ldc: int, col_offset: int) -> None:
+    """``int8_gemm_dequant_nk(A, B_nk, ...)`` stored straight into several fp16 matrices.
+
+    The ``[M, N]`` result goes to columns ``[col_offset, col_offset + N)`` of every
+    destination (device addresses in ``dst_ptrs``, 1 to 8 of them, each an fp16 matrix with row
+    pitch ``ldc`` elements, e.g. all ranks' replicated outputs of a column-sharded layer) in the
+    same launch; nothing is returned.  K must be a multiple of 16, ``ldc`` and ``col_offset``
+    multiples of 8 and every address 16-byte aligned.
+    """
+    M, N, K = _gemm_checks(A, B_nk, kn_layout=False)
+    dev = require_cuda("int8_gemm_dequant_scatter", A, B_nk, scale_a, scale_b)
+    require(K % 16 == 0, "K must be a multiple of 16")
+    require(scale_a.dtype == torch.float32 and scale_b.dtype == torch.float32, "scales must be fp32")
+    require(scale_a.numel() == M and scale_b.numel() == N, "scale_a must have M and scale_b N elements")
+    require(1 <= len(dst_ptrs) <= 8, "1 to 8 destinations")
+    require(ldc % 8 == 0 and col_offset % 8 == 0 and ldc >= col_offset + N, "ldc/col_offset must be multiples of 8 "
+            "and the block must fit in ldc")
+    if M == 0 or N == 0:
+        return
+    import ctypes
+
+    dsts = (ctypes.c_void_p * len(dst_ptrs))(*[int(p) for p in dst_ptrs])
+    _lib.call("lk_int8_gemm_dequant_scatter", ptr(A), K, ptr(B_nk), K, 1, ptr(scale_a.contiguous()),
+              ptr(scale_b.contiguous()), dsts, len(dst_ptrs), ldc, col_offset, M, N, K, stream_for(dev))
 
 
 def int8_gemm_i32(A: torch.Tensor, B: torch.Tensor, b_layout: str = "kn") -> torch.Tensor:

@@ -8,6 +8,12 @@ Every op shards without communication on its data path:
     ``all_gather_into_tensor`` -> ``shard_columns`` / ``gather_columns`` /
     ``column_sharded_int8_linear``.
 The gather is the only collective; it runs over NCCL on GPUs and over gloo in the CPU tests.
+
+``column_sharded_int8_linear_fused`` does the same layer with the gather inside the GEMM: each
+rank's epilogue stores its ``[M, N/g]`` tiles straight into every rank's replicated output
+(``PeerBuffers``: the peers' buffers mapped into this process with CUDA IPC, written over
+NVLink), so the transfer overlaps the GEMM tile by tile; two one-element NCCL all-reduces
+order the launch against the buffers' other users.
 """
 
 from __future__ import annotations
@@ -22,6 +28,8 @@ __all__ = [
     "shard_columns",
     "gather_columns",
     "column_sharded_int8_linear",
+    "PeerBuffers",
+    "column_sharded_int8_linear_fused",
 ]
 
 
@@ -94,3 +102,78 @@ def column_sharded_int8_linear(x: torch.Tensor, w_q_shard: torch.Tensor, scale_w
     xq, sx = quantize_symmetric(x)
     y = int8_gemm_dequant_nk(xq, w_q_shard, sx, scale_w_shard)
     return gather_columns(y, n_total, group) if replicate else y
+
+
+class PeerBuffers:
+    """One ``shape`` fp16 buffer per rank of ``group`` (one process per GPU), with every
+    peer's buffer mapped into this process: ``ptrs[r]`` is the device address of rank r's
+    buffer as seen from this rank's GPU (``ptrs[rank]`` is ``local``'s own address).  Kernels
+    on this GPU may store into all of them; NVLink carries the stores to the peers.
+
+    Collective: every rank constructs it with the same shape, in the same order.  Call
+    ``close()`` (also collective) before the process group is destroyed."""
+
+    def __init__(self, shape, group=None, dtype=torch.float16):
+        import ctypes
+
+        from . import _lib
+
+        world, rank = _world(group)
+        self.group, self.rank, self.world = group, rank, world
+        self.device = torch.cuda.current_device()
+        self.local = torch.empty(shape, dtype=dtype, device=f"cuda:{self.device}")
+        handle = (ctypes.c_char * _lib.LK_PEER_HANDLE_BYTES)()
+        off = ctypes.c_int64()
+        _lib.call("lk_peer_export", self.device, ctypes.c_void_p(self.local.data_ptr()), handle, ctypes.byref(off))
+        infos = [None] * world
+        dist.all_gather_object(infos, (bytes(handle), off.value), group=group)
+        self._opened = []
+        self.ptrs = []
+        for r in range(world):
+            if r == rank:
+                self.ptrs.append(self.local.data_ptr())
+                continue
+            h, o = infos[r]
+            p = ctypes.c_void_p()
+            _lib.call("lk_peer_open", self.device, ctypes.create_string_buffer(h, len(h)), o, ctypes.byref(p))
+            self.ptrs.append(p.value)
+            self._opened.append((p.value, o))
+
+    def close(self):
+        """Unmaps the peers' buffers once every rank is done with them (collective)."""
+        from . import _lib
+
+        if self._opened is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p, o in self._opened:
+            _lib.call("lk_peer_close", self.device, p, o)
+        self._opened = None
+
+
+def column_sharded_int8_linear_fused(x: torch.Tensor, w_q_shard: torch.Tensor, scale_w_shard: torch.Tensor,
+                                     out: PeerBuffers, group=None) -> torch.Tensor:
+    """``column_sharded_int8_linear`` with the gather fused into the GEMM epilogue.
+
+    ``out`` is a ``PeerBuffers`` of shape ``[M, N_total]``; rank r's columns are its
+    ``shard_range(N_total, r, g)`` and must start at a multiple of 8 (N_total a multiple of
+    8 * g does it).  Returns ``out.local``, the replicated ``[M, N_total]`` fp16 result, valid
+    on the current stream.  The all-reduce before the launch keeps a rank from overwriting a
+    peer's buffer that the peer is still reading; the one after it completes only when every
+    rank's stores have landed."""
+    from .int8_gemm import int8_gemm_dequant_scatter, quantize_symmetric
+
+    world, rank = _world(group)
+    M, n_total = out.local.shape
+    s, e = shard_range(n_total, rank, world)
+    if w_q_shard.shape[0] != e - s:
+        raise ValueError(f"rank {rank}: weight shard has {w_q_shard.shape[0]} rows, expected {e - s}")
+    if s % 8:
+        raise ValueError("column blocks must start at multiples of 8 (N_total a multiple of 8 * world)")
+    xq, sx = quantize_symmetric(x)
+    flag = torch.zeros(1, device=x.device)
+    dist.all_reduce(flag, group=group)
+    int8_gemm_dequant_scatter(xq, w_q_shard, sx, scale_w_shard, out.ptrs, n_total, s)
+    dist.all_reduce(flag, group=group)
+    return out.local

@@ -102,6 +102,33 @@ LK_API int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, i
 LK_API int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
                      int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* Column-sharded layer with the gather fused into the epilogue.  Computes this rank's
+ * [M, N] column block of dequant(A x B) exactly as lk_int8_gemm_dequant and stores every
+ * element into each of dsts[0 .. num_dst) at columns [col_offset, col_offset + N) of an
+ * fp16 matrix with row pitch ldc -- typically the replicated [M, N_total] outputs of all ranks,
+ * peers' buffers mapped with lk_peer_open, so the all-gather of the reference's optional
+ * tensor-parallel mode (an Int8Linear, llm_kernels/__init__.py:82-121, split by output
+ * columns) happens tile by tile inside the GEMM over NVLink instead of as a separate
+ * collective.  dsts is a host array of device pointers valid on the stream's device.
+ * 1 <= num_dst <= 8; ldc and col_offset multiples of 8; every dsts[d] 16-byte aligned.
+ * The caller orders the launch against the destinations' other users (e.g. a small NCCL
+ * all-reduce before and after, as llm_kernels.sharding does). */
+LK_API int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                                 const float* scale_a, const float* scale_b, void* const* dsts, int num_dst,
+                                 int64_t ldc, int64_t col_offset, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- peer buffers (CUDA IPC) -------------------------------------------------------------- *
+ * lk_peer_export writes an LK_PEER_HANDLE_BYTES-byte handle for the allocation holding ptr
+ * (on `device`) and ptr's byte offset inside it; another process passes both to lk_peer_open,
+ * which maps the allocation on its own `device` (peer access enabled on first use) and returns
+ * a pointer that kernels on that device can load from and store to.  lk_peer_close unmaps
+ * it.  A process cannot open its own handles.  No counterpart in the reference (its only
+ * multi-GPU path is the benchmark harness). */
+#define LK_PEER_HANDLE_BYTES 64
+LK_API int lk_peer_export(int device, const void* ptr, void* handle_out, int64_t* offset_out);
+LK_API int lk_peer_open(int device, const void* handle, int64_t offset, void** ptr_out);
+LK_API int lk_peer_close(int device, void* ptr, int64_t offset);
+
 /* ---- flash attention forward ------------------------------------------------------------ *
  * Replaces kernels/flash_attn/flash_attn_fwd.py:131-156 (flash_attn_forward) and its two
  * kernels (flash_attn_fwd.py:6-64 non-causal, :67-128 causal).

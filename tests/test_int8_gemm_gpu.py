@@ -149,3 +149,48 @@ def test_zero_and_degenerate_shapes():
     B = torch.zeros(64, 32, dtype=torch.int8, device="cuda")
     out = llm_kernels.int8_gemm_dequant_fwd(A, B, torch.ones(0, device="cuda"), torch.ones(32, device="cuda"))
     assert out.shape == (0, 32) and out.dtype == torch.float16
+
+
+# Scatter epilogue (the column-sharded layer's fused gather), on one GPU: the column block is
+# stored into two destination matrices at a column offset; both must equal the plain GEMM's
+# result bit for bit and the columns outside the block must stay untouched.  Shapes reach the
+# 1-CTA kernel (small), the CTA-pair kernel (2304 x 2048) and its split tail (4096 x 2048).
+@pytest.mark.parametrize("M,N,K,col0,ldc", [(300, 200, 256, 8, 512), (128, 256, 128, 0, 256), (2304, 2048, 512, 1024, 4096),
+                                             (4096, 2048, 4096, 2048, 4096), (77, 40, 48, 16, 64)])
+def test_scatter_epilogue_matches_plain_gemm(M, N, K, col0, ldc):
+    from llm_kernels.int8_gemm import int8_gemm_dequant_scatter
+
+    g = torch.Generator().manual_seed(M + N)
+    A = _rand_i8((M, K), 3 + M).cuda()
+    B = _rand_i8((N, K), 4 + N).cuda()
+    sa = (torch.rand(M, generator=g) * 0.02 + 1e-3).cuda()
+    sb = (torch.rand(N, generator=g) * 0.02 + 1e-3).cuda()
+    ref = llm_kernels.int8_gemm_dequant_nk(A, B, sa, sb)
+    dsts = [torch.full((M, ldc), 7.0, dtype=torch.float16, device="cuda") for _ in range(2)]
+    for _ in range(2):  # twice: the second launch must not depend on the first
+        int8_gemm_dequant_scatter(A, B, sa, sb, [d.data_ptr() for d in dsts], ldc, col0)
+    for d in dsts:
+        assert torch.equal(d[:, col0:col0 + N], ref)
+        outside = torch.cat([d[:, :col0], d[:, col0 + N:]], 1)
+        assert bool((outside == 7.0).all())
+
+
+def test_dequant_into_unaligned_output_through_the_c_abi():
+    """A C-ABI caller may pass an output that is only 2-byte aligned (here one fp16 element
+    into a buffer): the epilogue falls back to element stores instead of 16-byte ones."""
+    from llm_kernels import _lib
+    from llm_kernels._common import ptr, stream_for
+
+    M, N, K = 2304, 2304, 256  # CTA-pair kernel (C base not 16-byte aligned: no TMA store)
+    A = _rand_i8((M, K), 11).cuda()
+    B = _rand_i8((N, K), 12).cuda()
+    sa = torch.full((M,), 0.01, device="cuda")
+    sb = torch.full((N,), 0.02, device="cuda")
+    ref = llm_kernels.int8_gemm_dequant_nk(A, B, sa, sb)
+    for m, n in ((M, N), (200, 300)):  # and the 1-CTA kernel
+        buf = torch.zeros(m * N + 8, dtype=torch.float16, device="cuda")
+        out = buf[1:1 + m * N].view(m, N)
+        assert out.data_ptr() % 16 == 2
+        _lib.call("lk_int8_gemm_dequant", ptr(A[:m]), K, ptr(B[:n]), K, 1, ptr(sa[:m]), ptr(sb[:n]), ptr(out), N,
+                  m, n, K, stream_for(A.device))
+        assert torch.equal(out[:, :n], ref[:m, :n])

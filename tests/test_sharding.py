@@ -181,3 +181,50 @@ def test_column_sharded_path_on_gpu_world1_nccl():
         assert np.array_equal(y.cpu().numpy().view(np.uint16), ref.view(np.uint16))
     finally:
         dist.destroy_process_group()
+
+
+def _worker_fused_gather_gpu(rank, world, port, q):
+    """One rank of the column-sharded int8 linear on GPU `rank`: the fused-epilogue gather
+    (peer stores over NVLink) and the NCCL all-gather path must both equal the unsharded
+    Int8Linear bit for bit, on two calls in a row."""
+    try:
+        for p in (ROOT, PKG):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", store=store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device(f"cuda:{rank}"))
+        import llm_kernels
+        from llm_kernels.sharding import PeerBuffers, column_sharded_int8_linear, column_sharded_int8_linear_fused
+        from llm_kernels.sharding import shard_columns
+
+        results = []
+        for M, K, N in ((1000, 512, 768), (4096, 4096, 4096)):
+            g = torch.Generator().manual_seed(M + N)
+            x = torch.randn(M, K, generator=g).to(torch.float16).cuda()
+            w = torch.randn(N, K, generator=g).to(torch.float16).cuda()
+            layer = llm_kernels.Int8Linear(K, N).cuda()
+            layer.quantize_weights(w)
+            ref = layer(x)
+            wq_r = shard_columns(layer.w_q, rank, world)
+            sw_r = shard_columns(layer.scale_w[:, None], rank, world)[:, 0].contiguous()
+            buf = PeerBuffers((M, N))
+            for _ in range(2):
+                y = column_sharded_int8_linear_fused(x, wq_r, sw_r, buf)
+                results.append(bool(torch.equal(y, ref)))
+            results.append(bool(torch.equal(column_sharded_int8_linear(x, wq_r, sw_r, N), ref)))
+            buf.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok" if all(results) else f"mismatch {results}"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_column_sharded_fused_gather_on_two_gpus():
+    out = _run(_worker_fused_gather_gpu, world=2, timeout=240)
+    assert out == {0: "ok", 1: "ok"}, out
