@@ -347,25 +347,68 @@ def run_ours(args):
     launches = args.steps  # one fa_fwd_kernel launch per step
 
     # ---- end to end through the public API, host buffers (rank-local) ----
+    # Every step uploads its q, k, v from pinned host memory, runs flash_attn_forward and reads
+    # its output back into pinned host memory, all inside the timed region.  Steps alternate
+    # between two device buffer sets and the copies run on their own streams, so step i's
+    # upload overlaps step i-1's kernel and step i-2's download (PCIe moves both directions at
+    # once): how a serving loop would drive the op.
     qh = q.cpu().pin_memory()
     kh = k.cpu().pin_memory()
     vh = v.cpu().pin_memory()
-    oh = torch.empty_like(qh).pin_memory()
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    cur = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    sets = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(q)) for _ in range(2)]
+    ohs = [torch.empty_like(qh).pin_memory() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]  # set s may be refilled: its output has been read back
+    for ev in free:
+        ev.record(cur)
+    step_no = [0]
 
     def e2e_step():
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        o = llm_kernels.flash_attn_forward(qd, kd, vd, causal=True)
-        oh.copy_(o, non_blocking=True)
+        s_ = step_no[0] % 2
+        step_no[0] += 1
+        qd, kd, vd, od = sets[s_]
+        h2d.wait_event(free[s_])
+        with torch.cuda.stream(h2d):
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+        up = torch.cuda.Event()
+        up.record(h2d)
+        cur.wait_event(up)
+        llm_kernels.flash_attn_forward(qd, kd, vd, causal=True, out=od)
+        done = torch.cuda.Event()
+        done.record(cur)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            ohs[s_].copy_(od, non_blocking=True)
+        free[s_].record(d2h)
+
+    def e2e_time(steps_, warmup_):
+        for _ in range(warmup_):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        h2d.wait_stream(cur)  # the first timed upload starts after the start event
+        for _ in range(steps_):
+            e2e_step()
+        cur.wait_stream(d2h)  # the end event follows the last download
+        b.record(cur)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(a.elapsed_time(b), world)
 
     e2e_steps = max(3, args.steps // 4)
-    e2e_ms = time_loop(e2e_step, e2e_steps, 2, world) / e2e_steps
+    e2e_ms = e2e_time(e2e_steps, 2) / e2e_steps
     e2e_val = FLOPS_CAUSAL * world / (e2e_ms * 1e-3) / 1e12
     nbytes = q.numel() * q.element_size()
 
-    del qh, kh, vh, oh, qd, kd, vd
+    torch.cuda.synchronize()
+    del qh, kh, vh, sets, ohs
     decoder = decoder_layer_measure(args, llm_kernels, world, rank, dev)
 
     ops = {}
@@ -415,7 +458,9 @@ def run_ours(args):
             "algorithmic_bytes": 4 * nbytes,
         },
         "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * nbytes,
-                "d2h_bytes_per_step": nbytes},
+                "d2h_bytes_per_step": nbytes, "steps": e2e_steps,
+                "overlap": "two device buffer sets; uploads and downloads on their own streams overlap the "
+                           "neighbouring steps' kernels"},
         "gpu_launches": launches,
         "clocks": clk,
         "ops": ops,
