@@ -345,6 +345,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int n0 = n_base + c * 32;
         if (n0 >= p.N || m_warp >= p.M) return;
+        if constexpr (kEpi == Epi::DequantF16) {
+          if (p.num_dst > 0 && n0 + 32 <= p.N) {
+            // Scatter of a whole chunk: staged in this warp's store tile (same swizzle as the
+            // TMA path), then copied out so that every store instruction writes 8 rows x 64
+            // contiguous bytes to each destination -- full segments for the NVLink writes.
+            uint4 wv[8];
+            pack_chunk<kKind, kEpi>(r, row_scale, p, my_sb + c * 32, wv);
+            uint8_t* tile = my_cst + cbuf * 2048;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(tile + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = wv[q];
+            __syncwarp();
+            uint4 pc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
+              pc[i] = *reinterpret_cast<const uint4*>(tile + row * 64 + ((q ^ ((row >> 1) & 3)) << 4));
+            }
+            __syncwarp();  // the tile is free again for the next chunk
+#pragma unroll
+            for (int d = 0; d < kMaxScatter; ++d) {
+              if (d >= p.num_dst) break;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
+                if (m_warp + row < p.M)
+                  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 +
+                                            q * 8) = pc[i];
+              }
+            }
+            return;
+          }
+        }
         if (!p.c_tma) {
           if (row_ok) store_chunk<kKind, kEpi>(r, row_scale, m, n0, p, my_sb + c * 32);
           return;
