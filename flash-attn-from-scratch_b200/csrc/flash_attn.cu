@@ -32,6 +32,7 @@
 
 #include <atomic>
 
+#include "fa_common.cuh"
 #include "lk_abi.h"
 #include "lk_sm100.cuh"
 
@@ -75,6 +76,13 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   void* o;
   int64_t o_sb, o_sh, o_sm;  // element strides of O (d stride is 1)
+  // Optional log-sum-exp output (nullptr: none): lse[(b*H + h) * lse_ld + m] =
+  // ln(sum_n exp(scale * q_m . k_n)) over the visible keys.
+  float* lse;
+  int64_t lse_ld;
+  // Test hook (lk_debug_inject): CTA drop_block's producer skips ring item drop_item (no copy,
+  // no arrive).  drop_block = -1: none.
+  int drop_block, drop_item;
 };
 
 template <int D>
@@ -89,37 +97,6 @@ struct Cfg {
   static constexpr int kOCol0 = 256;
   static_assert(kStages >= 4, "K/V ring needs four stages");
 };
-
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// ---- packed fp32x2 arithmetic (one instruction for two lanes of the FMA pipe) ------------
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void uf2(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 
 // Max of n fp32 values (bit patterns): four chains of three-input max over sr[4 .. n-4), the
 // first and last four values opening and closing the chains.
@@ -137,17 +114,6 @@ __device__ __forceinline__ float row_max(const uint32_t (&sr)[n]) {
   mx4[0] = max3(mx4[0], __uint_as_float(sr[n - 4]), __uint_as_float(sr[n - 3]));
   mx4[1] = max3(mx4[1], __uint_as_float(sr[n - 2]), __uint_as_float(sr[n - 1]));
   return fmaxf(max3(mx4[0], mx4[1], mx4[2]), mx4[3]);
-}
-
-template <bool kBf16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  if constexpr (kBf16) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
-  } else {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
 }
 
 template <int D, bool kBf16>
@@ -250,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < C::kQBoxes; ++x)
           tma_load_4d(sQ + t * C::kTileBytes + x * (kTileM * 128), &tmQ, q_full, 64 * x, q0 + t * kTileM, h, b);
       // Ring order = MMA consumption order: item 2j = K_j, item 2j+1 = V_j.
+      const int drop = (p.drop_block == (int)blockIdx.x) ? p.drop_item : -1;
       int issued = 0;
       for (int i = 0; i < 2 * J && ok; ++i) {
         const int slot = i % S;
@@ -258,6 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (i == drop) {  // test hook: this item never arrives, its consumer's wait runs out
+          issued = i + 1;
+          continue;
+        }
         mbar_arrive_expect_tx(&kv_full[slot], C::kTileBytes);
         const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         const int row = (i >> 1) * kBlockN;
@@ -265,10 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < C::kQBoxes; ++x) tma_load_4d(dst + x * (kTileM * 128), tm, &kv_full[slot], 64 * x, row, hk, b);
         issued = i + 1;
       }
-      // Teardown: every copy issued must land before the CTA can exit.
-      mbar_wait(q_full, 0, kSiteTeardown);
+      // Teardown: every copy issued must land before the CTA can exit -- also after a failure,
+      // so these waits do not give up early when the status word is set.  A ring slot holds at
+      // most one unconsumed item, the last S items cover them all.
+      mbar_wait_drain(q_full, 0, kSiteTeardown);
       for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
-        mbar_wait(&kv_full[i % S], (i / S) & 1, kSiteTeardown);
+        if (i != drop) mbar_wait_drain(&kv_full[i % S], (i / S) & 1, kSiteTeardown);
     }
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
@@ -350,8 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         release_item(2 * j + 1);
         if (k_next) release_item(2 * j + 2);
       }
+      // Every MMA issued must be complete before tensor memory is freed.
       tc_commit(drain);
-      mbar_wait(drain, 0, kSiteTeardown);
+      mbar_wait_drain(drain, 0, kSiteTeardown);
     }
   } else {
     // ---------------------------------------------------------------- softmax (warps 0-7)
@@ -368,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < nb[t]; ++j) {
       // S_t(j) complete -- and with it PV_t(j-1), issued before it.
-      if (!mbar_wait(&s_full[t], j & 1, kSiteSoftS)) {
+      if (!mbar_wait_warp(&s_full[t], j & 1, kSiteSoftS)) {
         ok = false;
         break;
       }
@@ -401,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // where the other tile has no such block); each tile's turns complete in order, so
       // parities stay one phase apart.
       if (kExpTurns && (t == 0 ? (j >= 1 && j - 1 < nb[1]) : (j < nb[0]))) {
+        // Every lane polls the token in lockstep (no vote here: one costs registers in this
+        // loop); the waits whose outcome gates tensor-memory access are voted.
         if (!mbar_wait(&exp_tok[t], (t == 0 ? j - 1 : j) & 1, kSiteSoftS)) {
           ok = false;
           break;
@@ -464,9 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // of 64-column x 32-row boxes; rows past M are clipped by the copy.  Row-per-thread global
     // stores would touch 32 cache lines per instruction.
     if (ok && nb[t] > 0) {
-      if (mbar_wait(&o_full[t], 0, kSiteSoftO)) {
+      if (mbar_wait_warp(&o_full[t], 0, kSiteSoftO)) {
         tc_fence_after();
         const float inv = 1.f / l;
+        if (p.lse != nullptr && m < p.M) {
+          // l = sum_n 2^(x_n - m_used) with x = scale * log2(e) * s: ln(sum_n e^(scale * s_n))
+          // = (m_used + log2(l)) * ln(2).
+          p.lse[(int64_t)(b * p.H + h) * p.lse_ld + m] = (m_used + log2f(l)) * 0.69314718055994531f;
+        }
         uint8_t* stage = sQ + t * C::kTileBytes + quad * (32 * 128);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -524,7 +505,7 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, 
 }
 
 int make_map(CUtensorMap* map, bool bf16, const void* base, int64_t B, int64_t H, int64_t S, int64_t D,
-             const int64_t* st, uint32_t box_rows = 128) {
+             const int64_t* st, uint32_t box_rows) {
   if (st[3] != 1) return LK_ERR_INVALID_ARG;
   const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
   const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
@@ -544,12 +525,14 @@ extern "C" int lk_flash_attn_fwd(const void* q, const void* k, const void* v, vo
                                causal, softmax_scale, stream);
 }
 
-extern "C" int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, int dtype, int64_t B,
-                                     int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
-                                     const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
-                                     const int64_t* o_strides, int causal, float softmax_scale, void* stream) {
-  using namespace lk;
+namespace lk {
+namespace fa {
+int forward(const void* q, const void* k, const void* v, void* o, float* lse, int64_t lse_ld, int dtype, int64_t B,
+            int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, int causal,
+            float softmax_scale, void* stream) {
   if (B < 0 || H < 0 || M < 0 || N < 0) return LK_ERR_INVALID_ARG;
+  if (lse != nullptr && lse_ld < M) return LK_ERR_INVALID_ARG;
   if (H > 0 && (H_kv <= 0 || H % H_kv != 0)) return LK_ERR_INVALID_ARG;
   if (B == 0 || H == 0 || M == 0) return LK_OK;
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides || N == 0)
@@ -593,7 +576,34 @@ extern "C" int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v
   p.o_sb = o_strides[0];
   p.o_sh = o_strides[1];
   p.o_sm = o_strides[2];
+  p.lse = lse;
+  p.lse_ld = lse_ld;
+  {
+    const Injection inj = take_injection(LK_INJECT_FA_DROP_LOAD);
+    p.drop_block = inj.kind ? inj.block : -1;
+    p.drop_item = inj.item;
+  }
   if (D == 128)
     return bf16 ? fa::launch<128, true>(tq, tk, tv, to, p, s) : fa::launch<128, false>(tq, tk, tv, to, p, s);
   return bf16 ? fa::launch<64, true>(tq, tk, tv, to, p, s) : fa::launch<64, false>(tq, tk, tv, to, p, s);
+}
+}  // namespace fa
+}  // namespace lk
+
+extern "C" int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, int dtype, int64_t B,
+                                     int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
+                                     const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                     const int64_t* o_strides, int causal, float softmax_scale, void* stream) {
+  return lk::fa::forward(q, k, v, o, nullptr, 0, dtype, B, H, H_kv, M, N, D, q_strides, k_strides, v_strides,
+                         o_strides, causal, softmax_scale, stream);
+}
+
+extern "C" int lk_flash_attn_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse,
+                                     int64_t lse_ld, int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t M,
+                                     int64_t N, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                                     const int64_t* v_strides, const int64_t* o_strides, int causal,
+                                     float softmax_scale, void* stream) {
+  if (!lse && B > 0 && H > 0 && M > 0) return LK_ERR_INVALID_ARG;
+  return lk::fa::forward(q, k, v, o, lse, lse_ld, dtype, B, H, H_kv, M, N, D, q_strides, k_strides, v_strides,
+                         o_strides, causal, softmax_scale, stream);
 }

@@ -154,6 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (p.K + Cfg::kBK - 1) / Cfg::kBK;
+  // Producer state kept to the end of the kernel, where copies are drained after a failure.
+  uint32_t issued_mask = 0;       // stages this CTA has loaded into at least once
+  uint32_t last_parity_bits = 0;  // phase parity of the last load into each stage
+  bool prod_ok = true;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (both)
@@ -188,6 +192,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d_pair(dstB, &tmB, lbar, kx, n0);
           }
+          issued_mask |= 1u << stage;
+          last_parity_bits = (last_parity_bits & ~(1u << stage)) | (phase << stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -195,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) *(volatile int*)abort_flag = 1;
+      prod_ok = ok;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
@@ -247,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) *(volatile int*)abort_flag = 1;
       tc_commit_pair(cluster_addr(drain, 0));
-      mbar_wait(drain, 0, kSitePairTeardown);
+      mbar_wait_drain(drain, 0, kSitePairTeardown);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (both)
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSitePairAccFull)) break;
+      if (!mbar_wait_cluster_warp(&acc_full[acc], acc_phase, kSitePairAccFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * Cfg::kBN);
       // Split-tail role of this warp slot: a ticket below nwriters writes its partial, the
@@ -438,7 +445,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (writer) {
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicAdd(ready_ctr + widx * 8 + wslot, 1);
+        const bool skip = p.inj_kind == LK_INJECT_SPLIT_SKIP_PUBLISH && tail == p.inj_item && wslot == 0;
+        if (lane == 0 && !skip) atomicAdd(ready_ctr + widx * 8 + wslot, 1);
       }
       if (!ok) {
         *(volatile int*)abort_flag = 1;
@@ -462,6 +470,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // the even CTA's MMAs are drained: no peer smem is read after this
   tc_fence_after();
   if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  if (warp == 0 && lane == 0 && (!prod_ok || device_failed())) {
+    // After a failure some stages may never have been consumed, and nothing consumes or
+    // refills the ring any more.  Copies still in flight must land before their CTA exits.
+    // Both CTAs' copies into a stage complete on the even CTA's barrier, whose phase completes
+    // once both halves have landed: the even CTA waits for every stage it announced.  A copy
+    // the odd CTA issued into a phase the even CTA never announced completes no phase; the
+    // grace period covers it (a 16 KB copy lands in microseconds).  No cluster barrier follows:
+    // whether a CTA is on this path depends on when it read the status word.
+    if (leader)
+      for (int s = 0; s < S; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait_cluster_drain(&full[s], (last_parity_bits >> s) & 1u, kSitePairTeardown);
+    spin_ns(50000);
+  }
 }
 
 template <Kind kKind, bool kBMN, Epi kEpi>
@@ -480,6 +502,13 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMa
   }
   // Every unit (tile or split part) of the first round gets its own pair.
   const int pairs = p.num_units < num_sms / 2 ? p.num_units : num_sms / 2;
+  Params pl = p;
+  if (p.split > 1) {
+    const Injection inj = take_injection(LK_INJECT_SPLIT_SKIP_PUBLISH);
+    pl.inj_kind = inj.kind;
+    pl.inj_block = inj.block;
+    pl.inj_item = inj.item;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
@@ -494,7 +523,7 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMa
   attr[1].val.programmaticStreamSerializationAllowed = (kEpi == Epi::RowRsqrt) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
+  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, pl);
 }
 
 }  // namespace gemm

@@ -29,6 +29,7 @@
 #include <atomic>
 #include <type_traits>
 
+#include "lk_abi.h"
 #include "lk_sm100.cuh"
 
 namespace lk {
@@ -63,6 +64,11 @@ struct Params {
   // buffers mapped into this process over NVLink.
   void* c_dst[8];
   int num_dst;
+  // Test hooks armed by lk_debug_inject (inj_kind 0, the zero-initialised value, = none):
+  // LK_INJECT_GEMM_DROP_LOAD  the one-CTA kernel's CTA inj_block skips its inj_item-th stage load;
+  // LK_INJECT_SPLIT_SKIP_PUBLISH  the pair kernel's split-tail writer of leftover tile inj_item,
+  //                               warp slot 0, never publishes its partial.
+  int inj_kind, inj_block, inj_item;
 };
 constexpr int kMaxScatter = 8;
 
@@ -105,7 +111,10 @@ struct Config {
   static constexpr int kBBoxes = kBMN ? (BN * KT::kElemBytes) / 128 : 1;
   static constexpr int kBBoxBytes = kBMN ? kBK * 128 : kBBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+  // Per epilogue warp: one 32-row x 64-byte tile that stages a chunk for the scatter epilogue.
+  static constexpr int kScatterStageBytes = 4 * 2048;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kScatterStageBytes + 1024 /*align slack*/ +
+                                    256 /*barriers*/;
   static constexpr uint32_t kIdesc =
       make_idesc(KT::kCFmt, KT::kAFmt, KT::kBFmt, 0u, kBMN ? 1u : 0u, (uint32_t)kBM, (uint32_t)BN);
   static_assert(kMmasPerStage * KT::kMmaK == kBK, "stage must hold whole MMAs");
@@ -282,7 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* scatter_stage = smem + S * Cfg::kStageBytes;  // [4 warps][32 rows x 64 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(scatter_stage + Cfg::kScatterStageBytes);
   uint64_t* full = bars;               // [S]  TMA -> MMA
   uint64_t* empty = bars + S;          // [S]  MMA -> TMA (tcgen05.commit)
   uint64_t* acc_full = bars + 2 * S;   // [2]  MMA -> epilogue (tcgen05.commit)
@@ -321,15 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_kb = (p.K + Cfg::kBK - 1) / Cfg::kBK;
+  // Producer state kept to the end of the kernel, where copies are drained after a failure.
+  uint32_t issued_mask = 0;       // stages that have received at least one load
+  uint32_t last_parity_bits = 0;  // parity of the last load issued into each stage
+  bool prod_ok = true;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_mask = 0;       // stages that have received at least one load
-      uint32_t last_parity_bits = 0;  // parity of the last load issued into each stage
       bool ok = true;
+      const int drop = (p.inj_kind == LK_INJECT_GEMM_DROP_LOAD && p.inj_block == (int)blockIdx.x) ? p.inj_item : -1;
+      int nload = 0;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
@@ -342,6 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (*(volatile int*)abort_flag) {
             ok = false;
             break;
+          }
+          if (nload++ == drop) {  // test hook: this stage never fills, the MMA's wait runs out
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           const int kx = kb * kBKBytes / KT::kElemBytes;  // K element coordinate
@@ -363,12 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok) {
-        *(volatile int*)abort_flag = 1;
-        // Let every copy already issued land before the CTA can exit.
-        for (int s = 0; s < S; ++s)
-          if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_parity_bits >> s) & 1u, kSiteTeardownTma);
-      }
+      if (!ok) *(volatile int*)abort_flag = 1;
+      prod_ok = ok;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -422,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) *(volatile int*)abort_flag = 1;
       // Teardown: wait for every MMA issued by this thread before TMEM is released.
       tc_commit(drain);
-      mbar_wait(drain, 0, kSiteTeardownMma);
+      mbar_wait_drain(drain, 0, kSiteTeardownMma);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2-5)
@@ -447,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_phase, kSiteEpiAccFull)) break;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, kSiteEpiAccFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
@@ -462,6 +479,42 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
         const int n0 = n_base + c * 32;
+        if constexpr (kEpi == Epi::DequantF16) {
+          const int m_warp = mb * kBM + quad * 32;  // first row of this warp's 32
+          if (p.num_dst > 0 && n0 + 32 <= p.N && m_warp < p.M) {
+            // Scatter of a whole chunk (the column-sharded layer's fused gather): staged in this
+            // warp's tile (64-byte swizzle: piece q of row r at q ^ ((r >> 1) & 3)), then copied
+            // out so that every store instruction writes 8 rows x 64 contiguous bytes to each
+            // destination -- whole segments for the NVLink writes, where storing each lane's row
+            // from registers writes 32 scattered 16-byte pieces.
+            uint4 wv[8];
+            pack_chunk<kKind, kEpi>(r, row_scale, p, p.sb + n0, wv);
+            uint8_t* tile = scatter_stage + (warp - 2) * 2048;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(tile + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = wv[q];
+            __syncwarp();
+            uint4 pc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
+              pc[i] = *reinterpret_cast<const uint4*>(tile + row * 64 + ((q ^ ((row >> 1) & 3)) << 4));
+            }
+            __syncwarp();  // the tile is free again for the next chunk
+#pragma unroll
+            for (int d = 0; d < kMaxScatter; ++d) {
+              if (d >= p.num_dst) break;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
+                if (m_warp + row < p.M)
+                  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 +
+                                            q * 8) = pc[i];
+              }
+            }
+            continue;
+          }
+        }
         if (!row_ok || n0 >= p.N) continue;
         store_chunk<kKind, kEpi>(r, row_scale, m, n0, p, kEpi == Epi::DequantF16 ? p.sb + n0 : nullptr);
       }
@@ -473,6 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  if (warp == 0 && lane == 0 && (!prod_ok || device_failed())) {
+    // After a failure some stages may never have been consumed.  Every other role is done
+    // (past the barrier above), so nothing consumes or refills the ring any more: every copy
+    // issued lands and completes its stage's phase, and must before the CTA exits.
+    for (int s = 0; s < S; ++s)
+      if (issued_mask & (1u << s)) mbar_wait_drain(&full[s], (last_parity_bits >> s) & 1u, kSiteTeardownTma);
+  }
 }
 
 // ---- host side ----------------------------------------------------------------------------
@@ -491,6 +551,11 @@ int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Params& p, int 
     configured.fetch_or(bit);
   }
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
+  Params pl = p;
+  const Injection inj = take_injection(LK_INJECT_GEMM_DROP_LOAD);
+  pl.inj_kind = inj.kind;
+  pl.inj_block = inj.block;
+  pl.inj_item = inj.item;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -501,7 +566,7 @@ int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Params& p, int 
   attr[0].val.programmaticStreamSerializationAllowed = (kEpi == Epi::RowRsqrt) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+  return (int)cudaLaunchKernelEx(&cfg, kern, tmA, tmB, pl);
 }
 
 }  // namespace gemm

@@ -3,9 +3,6 @@
 
 #include <cuda_runtime.h>
 
-#include <map>
-#include <mutex>
-#include <utility>
 
 #include "gemm_sm100.cuh"
 
@@ -17,49 +14,26 @@ namespace lk {
 namespace gemm {
 
 // Workspace of the pair kernel's split tail, one per (device, stream): launches on one stream
-// never overlap, and each launch leaves its counters zero, so nothing is shared between
-// concurrent launches.  Sized for the most tail writers a launch can have (fewer than the
-// pairs): 256 KB of partials and 16 counters per pair.  Allocated on first use outside stream
-// capture; a launch captured before its stream has a workspace simply runs unsplit.
+// never overlap, and each launch that completes leaves its counters zero, so nothing is shared
+// between concurrent launches.  Sized for the most tail writers a launch can have (fewer than
+// the pairs): 256 KB of partials and 16 counters per pair.  Allocated on first use outside
+// stream capture; a launch captured before its stream has a workspace simply runs unsplit.
+// A launch that gave up (a bounded wait ran out, recorded in the device status word) can leave
+// counters non-zero; lk_clear_device_status re-zeroes the counters of every workspace of the
+// device, so split launches after the clear start from clean counters again.
 struct SplitWorkspace {
   uint4* partial = nullptr;
   int* flags = nullptr;
+  size_t flag_bytes = 0;
 };
 
-inline bool split_workspace(cudaStream_t stream, int npairs, SplitWorkspace* out) {
-  static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, SplitWorkspace> table;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = table.find(key);
-  if (it != table.end()) {
-    *out = it->second;
-    return true;
-  }
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return false;
-  }
-  SplitWorkspace ws;
-  const size_t partial_bytes = (size_t)npairs * 8 * 8 * 256 * sizeof(uint4);
-  const size_t flag_bytes = (size_t)npairs * 16 * sizeof(int);
-  if (cudaMalloc(&ws.partial, partial_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  if (cudaMalloc(&ws.flags, flag_bytes) != cudaSuccess || cudaMemsetAsync(ws.flags, 0, flag_bytes, stream) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(ws.partial);
-    if (ws.flags) cudaFree(ws.flags);
-    return false;
-  }
-  table[key] = ws;
-  *out = ws;
-  return true;
-}
+// Looks up (or, outside stream capture, creates) the workspace of (current device, stream).
+// Defined in lk_common.cu: one table for the whole library.
+bool split_workspace(cudaStream_t stream, int npairs, SplitWorkspace* out);
+
+// Synchronously zeroes the counters of every split workspace of the current device (the
+// device must be idle).  Returns a cudaError_t.
+int reset_split_workspaces();
 
 // Splits the tiles left over after whole rounds of `npairs` (all tiles, when there are fewer
 // than pairs) along K when that would leave pairs idle and the saved K blocks outweigh the

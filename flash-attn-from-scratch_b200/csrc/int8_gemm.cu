@@ -62,7 +62,7 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   if (lda < K || ldc < N) return LK_ERR_INVALID_ARG;
   if (b_mn ? (ldb < N) : (ldb < K)) return LK_ERR_INVALID_ARG;
   if (lda % 16 || ldb % 16) return LK_ERR_ALIGNMENT;
-  if (num_dst > 0 && (ldc % 8 || kEpi != Epi::DequantF16)) return LK_ERR_ALIGNMENT;
+  if (num_dst > 0 && (ldc % 8 || kEpi != Epi::DequantF16 || !aligned16(sb))) return LK_ERR_ALIGNMENT;
   for (int d = 0; d < num_dst; ++d)
     if (!aligned16(dsts[d])) return LK_ERR_ALIGNMENT;
   if (int st = bind_stream(stream)) return st;

@@ -16,7 +16,12 @@ int cuda_status(cudaError_t err);
 // cudaGetLastError() after a launch, mapped to a status.
 inline int check_launch() { return cuda_status(cudaGetLastError()); }
 
-// Makes the stream's device current in this library's runtime (no-op for the NULL stream).
+// Makes `dev` current in this library's runtime on the calling thread, with its primary
+// context (cached per thread).
+int bind_device(int dev);
+
+// Binds to the stream's device (for the NULL stream: to the device set with lk_set_device, or
+// device 0).
 int bind_stream(cudaStream_t stream);
 
 // Streaming multiprocessor count of the current device (cached per device).
@@ -29,5 +34,12 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void*
               CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Test-hook injection armed by lk_debug_inject.  take_injection(kind) returns it (and disarms
+// it) if it is of that kind; otherwise {LK_INJECT_NONE, -1, -1}.
+struct Injection {
+  int kind, block, item;
+};
+Injection take_injection(int kind);
 
 }  // namespace lk

@@ -33,11 +33,12 @@ enum DeviceCode : int {
   kDevTimeout = 4,  // matches LK_ERR_TIMEOUT in the public header
 };
 
-// Wait limit for every mbarrier wait, in nanoseconds of %globaltimer.  Legitimate waits in
-// these kernels are microseconds; a second means a lost arrive.
-#ifndef LK_WAIT_LIMIT_NS
-#define LK_WAIT_LIMIT_NS 1000000000ull
-#endif
+// Limit of every bounded wait, in nanoseconds of %globaltimer, per device (lk_common.cu).
+// Legitimate waits in these kernels are microseconds; the default second means a lost
+// arrive.  lk_debug_set_wait_limit lowers it for tests that make a wait run out on purpose.
+// Read only on a wait's slow path (after LK_WAIT_CHECK_MASK + 1 failed polls).
+extern __device__ unsigned long long g_wait_limit_ns;
+#define LK_WAIT_LIMIT_NS (*(volatile unsigned long long*)&::lk::g_wait_limit_ns)
 
 // Spins between two checks of the wall clock and of the grid-wide failure flag in a bounded
 // wait (the flag is a global load, so it is not read on every spin).
@@ -147,6 +148,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   }
 }
 
+// mbar_wait by every lane of a warp, with the outcome made warp-uniform: the warp-collective
+// tcgen05.ld / st that follow such a wait must be executed by all 32 lanes or by none.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, site));
+}
+
+// Bounded wait for a teardown: unlike mbar_wait it does not give up when another thread has
+// already recorded a failure, because what it waits for -- copies or MMAs this CTA issued that
+// still write its shared or tensor memory -- must be over before the CTA frees that memory or
+// exits.  Only the time limit ends it early (recording `site` if nothing failed before).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & LK_WAIT_CHECK_MASK) == 0 && globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
+      record_failure(kDevTimeout, site);
+      return false;
+    }
+  }
+}
+
+// Spins until `ns` nanoseconds of %globaltimer have passed (a bounded grace period for copies
+// whose completion no barrier phase this CTA can wait on will ever report).
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Proxy fences
 // ---------------------------------------------------------------------------------------------
@@ -175,6 +207,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completion counted on `bar`.  Both
+// addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -279,6 +321,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
 // tcgen05.wait::ld that also names the 32 destination registers of the load it waits for, so
@@ -400,6 +452,24 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
       }
     }
   }
+}
+
+// mbar_wait_drain with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster_drain(uint64_t* bar, uint32_t parity, int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & LK_WAIT_CHECK_MASK) == 0 && globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
+      record_failure(kDevTimeout, site);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity, int site) {
+  return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, site));
 }
 
 // TMA load into this CTA's shared memory whose completion is counted on the pair leader's

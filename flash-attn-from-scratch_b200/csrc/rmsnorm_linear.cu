@@ -15,6 +15,7 @@
 //                    warps start the main loop while the row kernel is still running; only
 //                    the epilogue waits (griddepcontrol.wait) before reading rstd.
 // The normalised activation is never written to HBM.
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -328,16 +329,43 @@ static __device__ __align__(256) float g_static_rstd[kStaticRstdRows];
 constexpr int kStaticDevices = 64;
 std::mutex g_static_mu;
 float* g_static_rstd_addr[kStaticDevices];
+unsigned long long g_static_rstd_ctx[kStaticDevices];  // unique id of the context it belongs to
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
 
+// Unique id (for the life of the process) of the calling thread's current context, 0 if none.
+unsigned long long current_context_id() {
+  if (!g_ctx_current || !g_ctx_id) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess || cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+        q2 != cudaDriverEntryPointSuccess)
+      return 0;
+    g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f1);
+    g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(f2);
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx || g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// The array's address, looked up once per device with that device current and kept with the
+// id of the context it was looked up in.  A device reset replaces the context (and the module
+// that holds the array), so a call in a new context looks the address up again.
 int static_rstd_address(float** out) {
   int dev = -1;
   if (int st = cuda_status(cudaGetDevice(&dev))) return st;
   if (dev < 0 || dev >= kStaticDevices) return LK_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_static_mu);
-  if (!g_static_rstd_addr[dev]) {
+  const unsigned long long id = current_context_id();
+  if (id == 0 || !g_static_rstd_addr[dev] || g_static_rstd_ctx[dev] != id) {
     void* p = nullptr;
     if (int st = cuda_status(cudaGetSymbolAddress(&p, g_static_rstd))) return st;
     g_static_rstd_addr[dev] = static_cast<float*>(p);
+    g_static_rstd_ctx[dev] = current_context_id();  // the lookup made the context current
   }
   *out = g_static_rstd_addr[dev];
   return LK_OK;

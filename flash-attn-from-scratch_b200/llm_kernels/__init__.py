@@ -9,6 +9,7 @@ kernels reached through the C ABI in ``include/llm_kernels_b200.h``.
 >>> out = llm_kernels.flash_attn_forward(q, k, v, causal=True)
 >>> out = llm_kernels.int8_gemm_dequant_fwd(A_q, B_q, sa, sb)
 >>> out = llm_kernels.fused_rmsnorm_linear(x, w_norm, w_lin)
+>>> out = llm_kernels.flash_attn_with_grad(q, k, v, causal=True); out.sum().backward()
 
 There is no CPU or PyTorch fallback: every op runs its CUDA kernel or raises.
 """
@@ -19,6 +20,7 @@ import torch.nn as nn
 from ._common import LKInputError
 from ._lib import LKError, device_status, clear_device_status
 from .flash_attn import flash_attn_forward
+from .flash_attn_bwd import FlashAttnFunction, flash_attn_forward_lse, flash_attn_with_grad
 from .fused_rmsnorm_linear import fused_rmsnorm_linear, fold_norm_weight, clear_fold_cache
 from .int8_gemm import (
     int8_gemm_dequant_fwd,
@@ -124,4 +126,8 @@ __all__ = [
     "FlashAttention",
     "FusedRMSNormLinear",
     "Int8Linear",
+    # training path (the reference's kernels/flash_attn/flash_attn_bwd.py)
+    "FlashAttnFunction",
+    "flash_attn_with_grad",
+    "flash_attn_forward_lse",
 ]

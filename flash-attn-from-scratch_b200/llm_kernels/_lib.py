@@ -26,6 +26,9 @@ LK_PEER_HANDLE_BYTES = 64  # include/llm_kernels_b200.h
 
 LK_F32, LK_F16, LK_BF16, LK_I8, LK_I32 = 0, 1, 2, 3, 4
 
+# Failure-path test hooks (lk_inject).
+LK_INJECT_NONE, LK_INJECT_FA_DROP_LOAD, LK_INJECT_GEMM_DROP_LOAD, LK_INJECT_SPLIT_SKIP_PUBLISH = 0, 1, 2, 3
+
 _p = ctypes.c_void_p
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -40,6 +43,8 @@ SIGNATURES = {
     "lk_set_device": (_i, [_i]),
     "lk_device_status": (_i, [ctypes.POINTER(ctypes.c_int)]),
     "lk_clear_device_status": (_i, []),
+    "lk_debug_set_wait_limit": (_i, [_i64]),
+    "lk_debug_inject": (_i, [_i, _i, _i]),
     "lk_quantize_symmetric": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "lk_int8_gemm_dequant": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "lk_int8_gemm_i32": (_i, [_p, _i64, _p, _i64, _i, _p, _i64, _i64, _i64, _i64, _p]),
@@ -56,6 +61,14 @@ SIGNATURES = {
     "lk_flash_attn_fwd_gqa": (
         _i,
         [_p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64, _i, _f, _p],
+    ),
+    "lk_flash_attn_fwd_lse": (
+        _i,
+        [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64, _i, _f, _p],
+    ),
+    "lk_flash_attn_bwd": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _i, _f, _p],
     ),
     "lk_rmsnorm_linear_fold": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _p]),
     "lk_rmsnorm_linear": (_i, [_p, _i64, _p, _p, _i64, _i, _i64, _i64, _i64, _f, _p, _p]),

@@ -159,9 +159,13 @@ def column_sharded_int8_linear_fused(x: torch.Tensor, w_q_shard: torch.Tensor, s
     ``out`` is a ``PeerBuffers`` of shape ``[M, N_total]``; rank r's columns are its
     ``shard_range(N_total, r, g)`` and must start at a multiple of 8 (N_total a multiple of
     8 * g does it).  Returns ``out.local``, the replicated ``[M, N_total]`` fp16 result, valid
-    on the current stream.  The all-reduce before the launch keeps a rank from overwriting a
-    peer's buffer that the peer is still reading; the one after it completes only when every
-    rank's stores have landed."""
+    on the current stream.  The all-reduce before the launch is ordered after the work already
+    queued on each rank's CURRENT stream, so it keeps a rank from overwriting a peer's buffer
+    while the peer's current stream still reads it; the one after it completes only when every
+    rank's stores have landed.  Every reader of ``out.local`` (and of an earlier result held in
+    it) must therefore run on the calling stream, or be ordered before this call on it (e.g. by
+    an event the caller records on its side stream and makes the current stream wait for):
+    peers' stores are not ordered against work on other streams."""
     from .int8_gemm import int8_gemm_dequant_scatter, quantize_symmetric
 
     world, rank = _world(group)

@@ -3,9 +3,13 @@
  *
  * Every entry point takes plain device pointers, 64-bit sizes/strides (in ELEMENTS), a dtype
  * code where the op is type-generic, and a cudaStream_t passed as `void*` (NULL = legacy
- * default stream).  Calls are asynchronous on that stream, never synchronise, never allocate
- * device memory, and return an lk_status code.  Argument errors are detected on the host
- * before anything is launched.
+ * default stream).  Compute calls are asynchronous on that stream and return an lk_status
+ * code; argument errors are detected on the host before anything is launched.  Outputs and
+ * scratch are caller-provided.  One exception allocates: the first int8 GEMM or
+ * lk_rmsnorm_linear call on a (device, stream) whose problem splits its last round of tiles
+ * allocates that stream's split workspace with cudaMalloc (which may synchronise the device)
+ * and keeps it until exit; see lk_int8_gemm_dequant.  lk_rmsnorm_linear_noalloc never
+ * allocates.  lk_device_status / lk_clear_device_status synchronise the device.
  *
  * Device-side failures (a pipeline wait that ran out of time) do not trap: the kernel records
  * the failure in a device status word and unwinds.  lk_device_status() reads that word
@@ -64,7 +68,36 @@ LK_API int lk_set_device(int device);
  * Returns out4[0] (or LK_ERR_CUDA). */
 LK_API int lk_device_status(int* out4);
 
-/* Resets the current device's status word to 0 (synchronous). */
+/* ---- failure-path test hooks (no counterpart in the reference, which has no device-side
+ * error path: kernels/flash_attn/flash_attn_fwd.py:132-135 only asserts on the host) ------ *
+ * They let a test make one bounded device wait run out on purpose and check that the kernel
+ * records LK_ERR_TIMEOUT, unwinds (in-flight copies and MMAs drained, tensor memory freed)
+ * and leaves the context usable.  Nothing faults: the hooks only withhold one copy or one
+ * counter update, so a consumer's bounded wait ends with an error status. */
+
+/* Limit of every bounded device wait on the current device, in nanoseconds (<= 0 restores the
+ * default of one second).  Synchronous. */
+LK_API int lk_debug_set_wait_limit(int64_t ns);
+
+/* Arms a one-shot injection, taken by the next launch of the named kernel in this process:
+ *   LK_INJECT_FA_DROP_LOAD        flash attention: the TMA producer of CTA `block` skips ring
+ *                                 item `item` (K_j = 2j, V_j = 2j+1): no copy, no arrive;
+ *   LK_INJECT_GEMM_DROP_LOAD      one-CTA GEMM (problems with fewer 256x256 tiles than SM
+ *                                 pairs): the producer of CTA `block` skips its `item`-th stage;
+ *   LK_INJECT_SPLIT_SKIP_PUBLISH  CTA-pair GEMM split tail: the writer warp of leftover tile
+ *                                 `item`, warp slot 0, never publishes its partial.
+ * kind LK_INJECT_NONE disarms. */
+typedef enum {
+  LK_INJECT_NONE = 0,
+  LK_INJECT_FA_DROP_LOAD = 1,
+  LK_INJECT_GEMM_DROP_LOAD = 2,
+  LK_INJECT_SPLIT_SKIP_PUBLISH = 3
+} lk_inject;
+LK_API int lk_debug_inject(int kind, int block, int item);
+
+/* Resets the current device's status word to 0 (synchronous), and re-zeroes the counters of
+ * every split workspace of the device, which a launch that gave up may have left non-zero.
+ * After a non-zero status, results of launches up to this call are not to be trusted. */
 LK_API int lk_clear_device_status(void);
 
 /* ---- quantize_symmetric ------------------------------------------------------------------ *
@@ -110,7 +143,8 @@ LK_API int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, int64
  * tensor-parallel mode (an Int8Linear, llm_kernels/__init__.py:82-121, split by output
  * columns) happens tile by tile inside the GEMM over NVLink instead of as a separate
  * collective.  dsts is a host array of device pointers valid on the stream's device.
- * 1 <= num_dst <= 8; ldc and col_offset multiples of 8; every dsts[d] 16-byte aligned.
+ * 1 <= num_dst <= 8; ldc and col_offset multiples of 8; every dsts[d] and scale_b 16-byte
+ * aligned.
  * The caller orders the launch against the destinations' other users (e.g. a small NCCL
  * all-reduce before and after, as llm_kernels.sharding does). */
 LK_API int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
@@ -121,9 +155,11 @@ LK_API int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const int8
  * lk_peer_export writes an LK_PEER_HANDLE_BYTES-byte handle for the allocation holding ptr
  * (on `device`) and ptr's byte offset inside it; another process passes both to lk_peer_open,
  * which maps the allocation on its own `device` (peer access enabled on first use) and returns
- * a pointer that kernels on that device can load from and store to.  lk_peer_close unmaps
- * it.  A process cannot open its own handles.  No counterpart in the reference (its only
- * multi-GPU path is the benchmark harness). */
+ * a pointer that kernels on that device can load from and store to.  lk_peer_close releases
+ * it.  Buffers carved out of one allocation share a handle: each (device, handle) is mapped
+ * once per process and counted, and its last lk_peer_close unmaps it.  A process cannot open
+ * its own handles.  No counterpart in the reference (its only multi-GPU path is the
+ * benchmark harness). */
 #define LK_PEER_HANDLE_BYTES 64
 LK_API int lk_peer_export(int device, const void* ptr, void* handle_out, int64_t* offset_out);
 LK_API int lk_peer_open(int device, const void* handle, int64_t offset, void** ptr_out);
@@ -155,6 +191,41 @@ LK_API int lk_flash_attn_fwd_gqa(const void* q, const void* k, const void* v, vo
                           const int64_t* q_strides, const int64_t* k_strides,
                           const int64_t* v_strides, const int64_t* o_strides,
                           int causal, float softmax_scale, void* stream);
+
+/* ---- flash attention: forward with log-sum-exp, and backward ----------------------------- *
+ * Replace the reference's training path kernels/flash_attn/flash_attn_bwd.py: its forward
+ * that also writes L (flash_attn_fwd_with_lse_kernel, :39-119), its backward kernel (:127-237)
+ * and the Delta pre-pass of FlashAttnFunction.backward (:293).  (Those reference kernels cannot
+ * run as written -- the head dimension D they use at :85 and :190 is never defined -- so they
+ * fix the formulas, not a tested behaviour.)
+ *
+ * lk_flash_attn_fwd_lse is lk_flash_attn_fwd_gqa that also writes, for every query row,
+ *     lse[(b*H + h) * lse_ld + m] = ln( sum_{visible n} exp(scale * <Q[b,h,m,:], K[b,h,n,:]>) )
+ * (the reference's L_i = m_i + log(l_i), flash_attn_bwd.py:118-119), fp32, lse_ld >= M.
+ *
+ * lk_flash_attn_bwd computes, for O = softmax(scale Q K^T [causal mask]) V and its upstream
+ * gradient dO (Q, O, dO, dQ [B, H, M, D]; K, V, dK, dV [B, H_kv, N, D], H_kv dividing H, query
+ * head h attending to K/V head h / (H / H_kv); dK, dV sum over the query heads sharing a head):
+ *     dV = P^T dO,  dS = P * (dO V^T - Delta),  dQ = scale dS K,  dK = scale dS^T Q,
+ * with P recomputed from lse (as written by lk_flash_attn_fwd_lse for the same Q, K, scale and
+ * mask) and Delta_m = sum_d dO[m,d] O[m,d], which it writes into the caller's `delta` scratch
+ * first.  Three kernels on `stream`: the Delta pass, a dK/dV pass over key tiles and a dQ pass
+ * over query tiles (no atomics: repeated calls give identical bits).
+ *   lse, delta: fp32 [B*H][lse_ld]; lse_ld a multiple of 4 and >= M rounded up to a multiple of
+ *               128 (whole 128-row tiles are read; values past M are ignored), 16-byte aligned.
+ *   strides:    32 element strides, (b, h, row, d) for q, k, v, o, dout, dq, dk, dv in that
+ *               order; d strides 1, the others multiples of 8; o, dout, dq, dk, dv 16-byte
+ *               aligned (read / written with 16-byte vectors).
+ * dtype LK_F16 or LK_BF16, D in {64, 128}, M, N >= 1 arbitrary, softmax_scale <= 0 = D^-0.5. */
+LK_API int lk_flash_attn_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse, int64_t lse_ld,
+                                 int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
+                                 const int64_t* q_strides, const int64_t* k_strides,
+                                 const int64_t* v_strides, const int64_t* o_strides,
+                                 int causal, float softmax_scale, void* stream);
+LK_API int lk_flash_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                             const float* lse, int64_t lse_ld, void* dq, void* dk, void* dv, float* delta,
+                             int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t M, int64_t N, int64_t D,
+                             const int64_t* strides, int causal, float softmax_scale, void* stream);
 
 /* ---- fused RMSNorm + Linear --------------------------------------------------------------- *
  * Replaces csrc/fused_rmsnorm_linear.cu:105-120 (launch_fused_rmsnorm_linear) behind
@@ -199,7 +270,8 @@ LK_API int lk_fused_rmsnorm_linear(const void* X, const void* W_norm, const void
  * The entry point itself calls no allocating function.
  *
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress)
- * and caches it; make that first call before any stream capture begins.  All calls on a
+ * and caches it with the device's current context (a call after a device reset looks it up
+ * again); make that first call before any stream capture begins.  All calls on a
  * device share the one array, so calls that can overlap on the GPU (different streams
  * without ordering between them) race on it; calls on one stream are ordered and safe.
  * Nothing in the array needs to start at zero: each call overwrites every value it reads. */

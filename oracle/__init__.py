@@ -13,7 +13,7 @@ see ``tests/golden/make_golden.py`` and ``tests/test_oracle_golden.py``.
 
 from .quantize import quantize_symmetric
 from .int8_gemm import int8_gemm_i32, dequant_f16, int8_gemm_dequant
-from .attention import attention_fp32, attention_gqa_fp32
+from .attention import attention_fp32, attention_gqa_fp32, attention_grad_fp32, attention_lse_fp32
 from .rmsnorm_linear import rmsnorm_linear_ref
 
 __all__ = [
@@ -23,5 +23,7 @@ __all__ = [
     "int8_gemm_dequant",
     "attention_fp32",
     "attention_gqa_fp32",
+    "attention_grad_fp32",
+    "attention_lse_fp32",
     "rmsnorm_linear_ref",
 ]

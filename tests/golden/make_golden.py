@@ -1,10 +1,12 @@
 """Generates the golden vectors in this directory by running the REFERENCE's own code.
 
-Run in a container that has the reference checkout (read-only) at /root/reference:
+Run where a checkout of the reference is available (read-only is enough), naming it with
+the first argument or the LK_REFERENCE_DIR environment variable:
 
-    python tests/golden/make_golden.py [/path/to/reference] [op ...]
+    python tests/golden/make_golden.py /path/to/reference [op ...]
+    LK_REFERENCE_DIR=/path/to/reference python tests/golden/make_golden.py [op ...]
 
-(op: quantize, int8_gemm, flash_attn, rmsnorm_linear, gqa; default all)
+(op: quantize, int8_gemm, flash_attn, flash_attn_bwd, rmsnorm_linear, gqa; default all)
 
 What it runs (all on the CPU):
   * ``quantize_symmetric``     kernels/int8_gemm/int8_gemm.py:146-161 (pure torch)
@@ -106,6 +108,35 @@ def make_flash_attn(ref):
     np.savez_compressed(os.path.join(HERE, "flash_attn.npz"), **out)
 
 
+def make_flash_attn_bwd(ref):
+    """The reference's training path, kernels/flash_attn/flash_attn_bwd.py: FlashAttnFunction
+    (:245-334) with its forward-with-LSE kernel (:39-119) and backward kernel (:127-237), both
+    interpreted.  As written the two kernels name the head dimension `D` without defining it
+    (:85, :190); the module-level name is bound to the inputs' head dimension here, which is
+    the only way they run.  Stored: the LSE of both modes and the non-causal dQ / dK / dV.  The
+    causal backward is not stored: its key-tile loop visits query tiles [0, (pid_n + 1) BLOCK_N)
+    (:200-202) -- the queries BEFORE the keys, which under the causal mask n <= m never see
+    them -- so its causal gradients are not the gradients of its causal forward."""
+    import kernels.flash_attn.flash_attn_bwd as bwd
+
+    out = {}
+    g = torch.Generator().manual_seed(16)
+    B, H, M, D = 1, 2, 128, 64
+    bwd.D = D
+    q, k, v, do = (torch.randn(B, H, M, D, generator=g).to(torch.float16) for _ in range(4))
+    out["q"], out["k"], out["v"], out["do"] = q.numpy(), k.numpy(), v.numpy(), do.numpy()
+    for causal in (0, 1):
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = bwd.FlashAttnFunction.apply(qq, kk, vv, bool(causal), 64, 64)
+        out[f"out_causal{causal}"] = o.detach().numpy()
+        out[f"lse_causal{causal}"] = o.grad_fn.saved_tensors[4].numpy()
+        if not causal:
+            o.backward(do)
+            out["dq_causal0"], out["dk_causal0"], out["dv_causal0"] = (
+                t.grad.numpy() for t in (qq, kk, vv))
+    np.savez_compressed(os.path.join(HERE, "flash_attn_bwd.npz"), **out)
+
+
 def make_rmsnorm_linear(ref):
     from kernels.fused_rmsnorm_linear.fused_ops import _rmsnorm_linear_ref
 
@@ -149,13 +180,19 @@ def make_gqa(ref):
 
 
 MAKERS = {"quantize": make_quantize, "int8_gemm": make_int8_gemm, "flash_attn": make_flash_attn,
-          "rmsnorm_linear": make_rmsnorm_linear, "gqa": make_gqa}
+          "flash_attn_bwd": make_flash_attn_bwd, "rmsnorm_linear": make_rmsnorm_linear, "gqa": make_gqa}
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    args = sys.argv[1:]
+    if args and os.path.isdir(args[0]):
+        ref, ops = args[0], args[1:]
+    else:
+        ref, ops = os.environ.get("LK_REFERENCE_DIR"), args
+    if not ref or not os.path.isdir(ref):
+        sys.exit("make_golden.py: name the reference checkout (first argument or LK_REFERENCE_DIR)")
     sys.path.insert(0, ref)
-    for name in sys.argv[2:] or list(MAKERS):
+    for name in ops or list(MAKERS):
         MAKERS[name](ref)
     print("golden vectors written to", HERE)
 

@@ -167,14 +167,34 @@ def test_large_logits_trigger_rescaling():
 
 @pytest.mark.parametrize("causal", [True, False])
 def test_config2_full_size_subset_of_heads(causal):
-    """Config 2 (B4 H32 N4096 D128 bf16, seed 1): the whole problem runs on the GPU; four
-    (b, h) slices are checked against the fp32 oracle on the CPU."""
+    """Config 2 (B4 H32 N4096 D128 bf16, seed 1): the whole problem runs on the GPU; sixteen
+    (b, h) slices -- every batch, heads spread over the CTA schedule's head groups, the
+    first and the last head (whose last q-block is the grid's last CTA) -- are checked
+    whole, all 4096 rows, against the fp32 oracle on the CPU with max-abs 1e-2."""
     q, k, v = _qkv(4, 32, 4096, 4096, 128, torch.bfloat16, 1)
     out = llm_kernels.flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal).cpu()
-    for b, h in ((0, 0), (1, 7), (2, 19), (3, 31)):
+    slices = [(0, 0), (0, 5), (0, 13), (0, 31), (1, 7), (1, 16), (1, 24), (1, 30),
+              (2, 2), (2, 11), (2, 19), (2, 27), (3, 0), (3, 9), (3, 22), (3, 31)]
+    for b, h in slices:
         sl = (slice(b, b + 1), slice(h, h + 1))
         ref = oracle.attention_fp32(q[sl], k[sl], v[sl], causal)
-        assert _err(out[sl], ref) <= ATOL
+        assert _err(out[sl], ref) <= ATOL, (b, h)
+
+
+@pytest.mark.parametrize("N", [2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("causal", [True, False])
+def test_config4_sweep_sizes(N, causal):
+    """Config 4 at the sizes the benchmark times: fp16, B8 H16 D64, scale 1/8, N = M up to
+    16384.  The whole problem runs on the GPU (inputs drawn there from a seeded generator);
+    three (b, h) slices -- the first, one in the middle and the last, whose last q-block is
+    the grid's last CTA -- are checked whole against the fp32 oracle, max-abs 1e-2."""
+    g = torch.Generator(device="cuda").manual_seed(3 + N)
+    q, k, v = (torch.randn(8, 16, N, 64, generator=g, device="cuda").to(torch.float16) for _ in range(3))
+    out = llm_kernels.flash_attn_forward(q, k, v, causal=causal, softmax_scale=0.125)
+    for b, h in ((0, 0), (4, 9), (7, 15)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        ref = oracle.attention_fp32(q[sl], k[sl], v[sl], causal, scale=0.125, row_block=2048)
+        assert _err(out[sl], ref) <= ATOL, (b, h)
 
 
 def test_module_wrapper_and_repr():

@@ -144,6 +144,22 @@ def test_int8_linear_module_matches_oracle():
     np.testing.assert_array_equal(y.cpu().numpy().view(np.uint16), ref.view(np.uint16))
 
 
+@pytest.mark.parametrize("M", [512, 1024, 1025, 2304])
+def test_auto_tile_heuristic_entry_point(M):
+    """int8_gemm_dequant_auto (kernels/int8_gemm/int8_gemm.py:192-200) picks 64^3 tiles for
+    M <= 1024 and 128x128x64 above; here both branches reach the same sm_100a GEMM and must
+    equal the oracle bit for bit (M = 2304 also takes the CTA-pair kernel)."""
+    N, K = 2304, 512
+    g = torch.Generator().manual_seed(31 + M)
+    A_q, sa = llm_kernels.quantize_symmetric(torch.randn(M, K, generator=g).to(torch.float16).cuda())
+    B_q, sb = llm_kernels.quantize_symmetric(torch.randn(N, K, generator=g).to(torch.float16).cuda())
+    B_kn = B_q.T.contiguous()
+    C = llm_kernels.int8_gemm_dequant_auto(A_q, B_kn, sa, sb)
+    ref = oracle.int8_gemm_dequant(A_q.cpu().numpy(), B_kn.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy(), "kn")
+    assert C.shape == (M, N) and C.dtype == torch.float16
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
 def test_zero_and_degenerate_shapes():
     A = torch.zeros(0, 64, dtype=torch.int8, device="cuda")
     B = torch.zeros(64, 32, dtype=torch.int8, device="cuda")

@@ -110,3 +110,49 @@ def test_golden_vectors_reject_a_planted_rounding_mistake():
     assert not np.array_equal(wrong[4], g["f32_special_q"][4])
     q, _ = oracle.quantize_symmetric(torch.from_numpy(x))
     np.testing.assert_array_equal(q, g["f32_special_q"])
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_attention_lse_vs_reference_forward_with_lse(causal):
+    """The LSE the reference's forward-with-LSE kernel stores (flash_attn_bwd.py:118-119)."""
+    g = _load("flash_attn_bwd")
+    q, k, v = (torch.from_numpy(g[n]) for n in ("q", "k", "v"))
+    lse = oracle.attention_lse_fp32(q, k, v, bool(causal))
+    assert (lse - torch.from_numpy(g[f"lse_causal{causal}"])).abs().max().item() <= 2e-3
+    out = oracle.attention_fp32(q, k, v, bool(causal))
+    assert (out - torch.from_numpy(g[f"out_causal{causal}"]).float()).abs().max().item() <= 1e-2
+
+
+def test_attention_grad_vs_reference_backward_kernel():
+    """dQ, dK, dV of the reference's backward kernel (flash_attn_bwd.py:127-237, fp16 operands,
+    fp16 atomics for dQ) on the non-causal case; the reference's causal loop bounds are wrong
+    (make_golden.make_flash_attn_bwd), so only the non-causal gradients pin the oracle."""
+    g = _load("flash_attn_bwd")
+    q, k, v, do = (torch.from_numpy(g[n]) for n in ("q", "k", "v", "do"))
+    dq, dk, dv = oracle.attention_grad_fp32(q, k, v, do, False)
+    for name, got in (("dq", dq), ("dk", dk), ("dv", dv)):
+        ref = torch.from_numpy(g[f"{name}_causal0"]).float()
+        assert (got - ref).abs().max().item() <= 5e-3, name
+
+
+def test_attention_grad_is_the_gradient_of_the_oracle_forward():
+    """Finite differences of sum(O * dO) against the oracle's gradients (fp64 inputs), causal
+    and not, with fewer K/V heads than Q heads: the gradients are those of attention_fp32 /
+    attention_gqa_fp32."""
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(1, 4, 9, 8, generator=g, dtype=torch.float64)
+    k = torch.randn(1, 2, 11, 8, generator=g, dtype=torch.float64)
+    v = torch.randn(1, 2, 11, 8, generator=g, dtype=torch.float64)
+    do = torch.randn(1, 4, 9, 8, generator=g, dtype=torch.float64)
+    for causal in (False, True):
+        dq, dk, dv = oracle.attention_grad_fp32(q, k, v, do, causal)
+        f = lambda qq, kk, vv: (oracle.attention_gqa_fp32(qq, kk, vv, causal) * do.float()).sum().item()  # noqa: E731
+        for t, grad, idx in ((q, dq, (0, 3, 8, 5)), (k, dk, (0, 1, 4, 2)), (v, dv, (0, 0, 10, 7))):
+            e = 1e-2
+            tp, tm = t.clone(), t.clone()
+            tp[idx] += e
+            tm[idx] -= e
+            args_p = [tp if t is x else x for x in (q, k, v)]
+            args_m = [tm if t is x else x for x in (q, k, v)]
+            fd = (f(*args_p) - f(*args_m)) / (2 * e)
+            assert abs(fd - grad[idx].item()) <= 2e-3 * max(1.0, abs(fd)), (causal, idx)

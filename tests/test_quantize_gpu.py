@@ -97,3 +97,20 @@ def test_quantize_full_size_4096sq():
 def test_quantize_empty_rows():
     q, s = llm_kernels.quantize_symmetric(torch.empty(0, 64, device="cuda", dtype=torch.float16))
     assert q.shape == (0, 64) and s.shape == (0,)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_quantize_many_rows_specials_and_strides(dtype):
+    """Thousands of 1024-wide rows (many waves of CTAs), fewer rows than SMs, rows holding
+    zeros / inf / NaN / subnormals, and a row stride larger than the row."""
+    g = torch.Generator().manual_seed(41)
+    x = (torch.randn(6000, 1024, generator=g) * 3).to(dtype)
+    x[5] = 0.0
+    x[77, 3] = float("inf")
+    x[1000, 9] = float("nan")
+    x[4321, :] = 1e-40 if dtype == torch.float32 else 0.0
+    x[5999, 100] = -float("inf")
+    _check(x.cuda())
+    _check(x[:100].cuda())
+    wide = (torch.randn(40, 3000, generator=g) * 0.01).to(dtype).cuda()
+    _check(wide[:, :2048])  # row stride 3000 elements, 16-byte multiple for every dtype

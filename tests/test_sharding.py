@@ -216,7 +216,16 @@ def _worker_fused_gather_gpu(rank, world, port, q):
                 y = column_sharded_int8_linear_fused(x, wq_r, sw_r, buf)
                 results.append(bool(torch.equal(y, ref)))
             results.append(bool(torch.equal(column_sharded_int8_linear(x, wq_r, sw_r, N), ref)))
+            # A second set of buffers while the first is open: on a peer both usually sit in one
+            # caching-allocator segment, i.e. arrive with the same IPC handle.  Closing the first
+            # must leave the second mapped.
+            buf2 = PeerBuffers((M, N))
+            y2 = column_sharded_int8_linear_fused(x, wq_r, sw_r, buf2)
+            results.append(bool(torch.equal(y2, ref)))
             buf.close()
+            y2 = column_sharded_int8_linear_fused(x, wq_r, sw_r, buf2)
+            results.append(bool(torch.equal(y2, ref)))
+            buf2.close()
         dist.destroy_process_group()
         q.put((rank, "ok" if all(results) else f"mismatch {results}"))
     except Exception:
@@ -225,6 +234,9 @@ def _worker_fused_gather_gpu(rank, world, port, q):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_column_sharded_fused_gather_on_two_gpus():
-    out = _run(_worker_fused_gather_gpu, world=2, timeout=240)
-    assert out == {0: "ok", 1: "ok"}, out
+def test_column_sharded_fused_gather_on_all_gpus():
+    """Every GPU of the box (2 to 8) as one rank: per-rank column blocks of 384 / 192 / 96
+    (one-CTA kernel) and 2048 / 1024 / 512 columns (CTA-pair kernel at 2 ranks)."""
+    world = min(torch.cuda.device_count(), 8)
+    out = _run(_worker_fused_gather_gpu, world=world, timeout=300)
+    assert out == {r: "ok" for r in range(world)}, out
