@@ -9,6 +9,8 @@
 
 #include <cstdint>
 
+#include "lk_sm100.cuh"
+
 namespace lk {
 namespace fa {
 
@@ -18,30 +20,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// ---- packed fp32x2 arithmetic (one instruction for two lanes of the FMA pipe) ------------
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void uf2(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
+// Packed fp32x2 arithmetic lives in lk_sm100.cuh.
+using lk::add2;
+using lk::f2;
+using lk::fma2;
+using lk::max3;
+using lk::uf2;
 
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {

@@ -34,6 +34,7 @@
 #pragma once
 
 #include "gemm_sm100.cuh"
+#include "quant_common.cuh"
 
 namespace lk {
 namespace gemm {
@@ -55,7 +56,8 @@ struct PairConfig {
   static constexpr int kSbStageBytes = 4 * 256 * 4;  // per epilogue warp: the tile's 256 column scales
   // Per epilogue warp: two 2 KB store tiles of 32 rows x 64 bytes (64-byte swizzle) for TMA stores of C.
   static constexpr int kCStageBytes = 4 * 2 * 2048;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kCStageBytes + 1024 + 256 + kSbStageBytes;
+  static constexpr int kBarBytes = 512;  // mbarriers, TMEM slot, abort flag
+  static constexpr int kSmemBytes = kStages * kStageBytes + kCStageBytes + 1024 + kBarBytes + kSbStageBytes;
   static constexpr uint32_t kIdesc =
       make_idesc(KT::kCFmt, KT::kAFmt, KT::kBFmt, 0u, kBMN ? 1u : 0u, 2u * kBM, (uint32_t)kBN);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -68,7 +70,28 @@ enum PairSite : int {
   kSitePairAccFull = 124,
   kSitePairTeardown = 125,
   kSitePairSplit = 126,
+  kSitePairRequant = 127,
 };
+
+// Bounded wait until *ctr >= target, polling L2 every ~0.1 us (many warps may poll one
+// counter); records a timeout at `site` and returns false when it runs out.
+__device__ __forceinline__ bool wait_count_sleep(const int* ctr, int target, int site) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_gpu(ctr) < target) {
+    __nanosleep(128);
+    if (device_failed()) return false;
+    if (globaltimer_ns() - t0 > LK_WAIT_LIMIT_NS) {
+      record_failure(kDevTimeout, site);
+      return false;
+    }
+  }
+  return true;
+}
+
+// The re-quantising epilogue runs two more warps (its second pass, two TMEM quadrants each):
+// 8 warps keep two warps per SM sub-partition, so a thread may use up to 255 registers.
+__host__ __device__ constexpr int pair_threads(Epi e) { return e == Epi::DequantQuant ? 256 : kThreads; }
 
 struct Unit {
   int tile, kb0, kb1, part;  // part < 0: the whole tile
@@ -96,7 +119,7 @@ __device__ __forceinline__ Unit decode_unit(int u, const Params& p, int num_kb) 
 }
 
 template <Kind kKind, bool kBMN, Epi kEpi>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(pair_threads(kEpi), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const Params p) {
   using Cfg = PairConfig<kKind, kBMN>;
@@ -117,7 +140,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* sb_stage = reinterpret_cast<float*>(c_stage + Cfg::kCStageBytes + 256);  // [4 warps][256]
+  float* sb_stage = reinterpret_cast<float*>(c_stage + Cfg::kCStageBytes + Cfg::kBarBytes);  // [4 warps][256]
+  // DequantQuant: parked-tile handoff between the pass-1 and pass-2 warps of a TMEM quadrant.
+  uint64_t* parked_full = reinterpret_cast<uint64_t*>(c_stage + Cfg::kCStageBytes + 256);  // [4 quads][2 slots]
+  uint64_t* parked_empty = parked_full + 8;                                                 // [4 quads][2 slots]
 
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
@@ -134,6 +160,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 8);
+    }
+    if (kEpi == Epi::DequantQuant) {
+      for (int i = 0; i < 8; ++i) {
+        mbar_init(&parked_full[i], 1);
+        mbar_init(&parked_empty[i], 1);
+      }
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -256,6 +288,106 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit_pair(cluster_addr(drain, 0));
       mbar_wait_drain(drain, 0, kSitePairTeardown);
     }
+  } else if (kEpi == Epi::DequantQuant && warp >= 6) {
+    // ------------------------------------------------------------------ codes (DequantQuant, both)
+    // Pass 2 of the re-quantising epilogue; warp 6 serves TMEM quadrants 0-1, warp 7 quadrants
+    // 2-3.  Per tile and quadrant: take the parked tile, wait until every tile of its row block
+    // has published its row maxima, write the int8 codes and the row scales, hand the slot back.
+    // A tile waits only for tiles of its own row block, which the host keeps within 2 * pairs
+    // consecutive tiles, so every wait points at work that does not depend on it (and all
+    // waits are bounded).
+    uint8_t* my_cst = c_stage + (warp - 6) * 4096;
+    int cbuf = 0;
+    int lt = 0;
+    bool ok = true;
+    for (int u = pair; u < p.num_units && ok; u += npairs, ++lt) {
+      const Unit w = decode_unit(u, p, num_kb);
+      int mb, nb;
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, mb, nb, p.group_m);
+      const int n_base = nb * Cfg::kBN;
+      const int slot = lt & 1;
+#pragma unroll 1
+      for (int qi = 0; qi < 2; ++qi) {
+        const int quad = (warp - 6) * 2 + qi;
+        const int m_warp = mb * kPairM + (int)rank * kBM + quad * 32;
+        const int m = m_warp + lane;
+        const bool row_ok = m < p.M;
+        if (!mbar_wait_warp(&parked_full[quad * 2 + slot], (lt >> 1) & 1, kSitePairRequant)) {
+          ok = false;
+          break;
+        }
+        const uint4* slot_base = p.q_park + (size_t)(blockIdx.x * 4 + quad) * 2048 + slot * 1024;
+        // The whole parked row (256 fp16 values) in flight at once, while the row block's
+        // maxima are awaited: one L2 round trip per tile and quadrant.
+        uint4 pv[32];
+        if (m_warp < p.M) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pv[i] = __ldcg(slot_base + i * 32 + lane);
+          int g = 1;
+          if (lane == 0) g = wait_count_sleep(p.q_slice_ctr + (m_warp >> 5), p.tiles_n, kSitePairRequant) ? 1 : 0;
+          if (__shfl_sync(0xffffffffu, g, 0) == 0) {
+            ok = false;
+            break;
+          }
+          RowScale rs;
+          rs.scale = 0.f;
+          rs.rcp = 0.f;
+          rs.fast = false;
+          if (row_ok) {
+            const uint32_t amax = (uint32_t)ld_acquire_gpu(reinterpret_cast<const int*>(p.q_absmax + m));
+            rs = make_row_scale(__half2float(__ushort_as_half((unsigned short)amax)));
+            if (nb == 0) p.q_scale[m] = rs.scale;
+          }
+#pragma unroll
+          for (int st = 0; st < Cfg::kBN / 64; ++st) {
+            const int x0 = n_base + st * 64;
+            if (x0 >= p.N) break;
+            uint32_t words[16];  // the codes of columns x0 .. x0+63 of this lane's row
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint64_t x2[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 q = pv[(2 * st + h) * 4 + j];
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+                  x2[4 * j + e] = f2(f.x, f.y);
+                }
+              }
+              uint32_t b[32];
+              codes_x2<16>(x2, rs, b);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                words[h * 8 + j] = pack4_codes(b[4 * j], b[4 * j + 1], b[4 * j + 2], b[4 * j + 3]);
+            }
+            // 32 rows x 64 codes through this warp's store tile (64-byte swizzle) and one TMA
+            // store; rows past M and columns past N are clipped by the copy.
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            uint8_t* tile = my_cst + cbuf * 2048;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(tile + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(words[4 * q], words[4 * q + 1], words[4 * q + 2], words[4 * q + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, tile, x0, m_warp);
+              bulk_commit_group();
+            }
+            cbuf ^= 1;
+          }
+        }
+        __syncwarp();  // every parked value of this slot has been read
+        if (lane == 0) mbar_arrive(&parked_empty[quad * 2 + slot]);
+      }
+      if (*(volatile int*)abort_flag) break;
+    }
+    if (!ok) *(volatile int*)abort_flag = 1;
+    if (lane == 0) bulk_wait_group<0>();  // code stores complete before shared memory goes
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue (both)
     const int quad = warp & 3;
@@ -267,6 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* my_sb = sb_stage + (warp - 2) * 256;
     uint8_t* my_cst = c_stage + (warp - 2) * 4096;
     int cbuf = 0;  // next store tile of this warp
+    // DequantQuant: this quadrant's ring of two parked fp16 tiles (32 rows x 256 columns each),
+    // filled here (pass 1) and drained by the quadrant's codes warp (pass 2).
+    uint4* park = (kEpi == Epi::DequantQuant) ? p.q_park + (size_t)(blockIdx.x * 4 + quad) * 2048 : nullptr;
     int local = 0;
     for (int u = pair; u < p.num_units; u += npairs, ++local) {
       const Unit w = decode_unit(u, p, num_kb);
@@ -277,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_base = nb * Cfg::kBN;
       const bool row_ok = m < p.M;
       float row_scale = 0.f;
-      if constexpr (kEpi == Epi::DequantF16) {
+      if constexpr (kEpi == Epi::DequantF16 || kEpi == Epi::DequantQuant) {
         row_scale = row_ok ? __ldg(p.sa + m) : 0.f;
         // The tile's column scales go to this warp's shared slice while the MMAs run, so the
         // chunk loop below reads them without a round trip to L2.  (The warp finished reading
@@ -297,6 +432,87 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_cluster_warp(&acc_full[acc], acc_phase, kSitePairAccFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * Cfg::kBN);
+      if constexpr (kEpi == Epi::DequantQuant) {
+        // Pass 1 of this tile: dequantise each 32-column chunk, round it to fp16 (writing C if
+        // asked), take this row's max magnitude and park the fp16 values in this warp's ring
+        // slot (L2-resident); the accumulator goes back to the MMA warp as soon as its last
+        // chunk is in registers.  Then publish the row maxima, and write the codes of the
+        // PREVIOUS tile (pass 2), whose row block has normally finished its pass 1 by now.
+        constexpr int kChunks = Cfg::kBN / 32;
+        uint32_t mag2 = 0;  // two fp16 magnitude maxima, packed
+        const int slot = local & 1;
+        // The codes warp has drained this slot's previous tile.
+        if (!mbar_wait_warp(&parked_empty[quad * 2 + slot], ((local >> 1) & 1) ^ 1u, kSitePairRequant)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        uint4* slot_base = park + slot * 1024;
+        auto pass1 = [&](int c, const uint32_t(&r)[32]) {
+          float v[32];
+          chunk_values<kKind, Epi::DequantF16>(r, row_scale, 0, p, my_sb + c * 32, true, v);
+          uint32_t hw[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            hw[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+            mag2 = __vmaxu2(mag2, hw[j] & 0x7FFF7FFFu);
+          }
+          // Slot layout [chunk][4][32 lanes] of 16 bytes: each store writes 512 contiguous bytes.
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            __stcg(slot_base + (c * 4 + j) * 32 + lane, make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]));
+          const int n0 = n_base + c * 32;
+          if (p.C != nullptr && row_ok && n0 < p.N) {
+            uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)m * p.ldc + n0;
+            if (n0 + 32 <= p.N && (p.ldc % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(crow)[j] = make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N) crow[j] = (uint16_t)((j & 1) ? (hw[j >> 1] >> 16) : (hw[j >> 1] & 0xFFFFu));
+            }
+          }
+        };
+        {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(t_row, ra);
+          tmem_wait_ld_regs(ra);
+#pragma unroll 1
+          for (int c = 0; c < kChunks; c += 2) {
+            tmem_ld32(t_row + (c + 1) * 32, rb);
+            pass1(c, ra);
+            tmem_wait_ld_regs(rb);
+            if (c + 2 < kChunks) {
+              tmem_ld32(t_row + (c + 2) * 32, ra);
+            } else {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (leader)
+                  mbar_arrive(&acc_empty[acc]);
+                else
+                  mbar_arrive_remote(&acc_empty[acc], 0);
+              }
+            }
+            pass1(c + 1, rb);
+            if (c + 2 < kChunks) tmem_wait_ld_regs(ra);
+          }
+        }
+        if (m_warp < p.M) {
+          const uint32_t mag = max(mag2 & 0xFFFFu, mag2 >> 16);
+          if (row_ok) atomicMax(p.q_absmax + m, mag);
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence();  // the warp's maxima are visible before the count that announces them
+            atomicAdd(p.q_slice_ctr + (m_warp >> 5), 1);
+          }
+        }
+        __threadfence_block();  // parked values visible to the codes warp before the handoff
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&parked_full[quad * 2 + slot]);
+        if (*(volatile int*)abort_flag) break;
+        continue;
+      }
       // Split-tail role of this warp slot: a ticket below nwriters writes its partial, the
       // last ticket finishes the tile.
       const int tail = w.tile - p.full_tiles;
@@ -487,21 +703,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <Kind kKind, bool kBMN, Epi kEpi>
-int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const Params& p, int num_sms,
-                cudaStream_t stream) {
+cudaError_t configure_pair() {
   using Cfg = PairConfig<kKind, kBMN>;
-  auto kern = gemm_pair_kernel<kKind, kBMN, kEpi>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    if (e != cudaSuccess) return (int)e;
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<kKind, kBMN, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
+  return cudaSuccess;
+}
+
+// How many CTA pairs of this kernel the device can hold at once (<= SMs / 2).
+template <Kind kKind, bool kBMN, Epi kEpi>
+cudaError_t resident_pairs(int num_sms, int* out) {
+  using Cfg = PairConfig<kKind, kBMN>;
+  if (cudaError_t e = configure_pair<kKind, kBMN, kEpi>()) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms & ~1);
+  cfg.blockDim = dim3(pair_threads(kEpi));
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<kKind, kBMN, kEpi>, &cfg)) return e;
+  *out = n < num_sms / 2 ? n : num_sms / 2;
+  return cudaSuccess;
+}
+
+// max_pairs > 0 caps the grid (the re-quantising epilogue needs every pair resident at once).
+template <Kind kKind, bool kBMN, Epi kEpi>
+int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const Params& p, int num_sms,
+                cudaStream_t stream, int max_pairs = 0) {
+  using Cfg = PairConfig<kKind, kBMN>;
+  auto kern = gemm_pair_kernel<kKind, kBMN, kEpi>;
+  if (cudaError_t e = configure_pair<kKind, kBMN, kEpi>()) return (int)e;
   // Every unit (tile or split part) of the first round gets its own pair.
-  const int pairs = p.num_units < num_sms / 2 ? p.num_units : num_sms / 2;
+  int pairs = p.num_units < num_sms / 2 ? p.num_units : num_sms / 2;
+  if (max_pairs > 0 && pairs > max_pairs) pairs = max_pairs;
   Params pl = p;
   if (p.split > 1) {
     const Injection inj = take_injection(LK_INJECT_SPLIT_SKIP_PUBLISH);
@@ -511,7 +759,7 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMa
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(pair_threads(kEpi));
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];

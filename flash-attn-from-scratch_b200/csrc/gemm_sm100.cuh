@@ -40,6 +40,10 @@ enum class Epi : int {
   DequantF16 = 0,  // C fp16 = fp16((fp32(acc) * sa[m]) * sb[n])
   RawI32 = 1,      // C int32 = acc
   RowRsqrt = 2,    // C (f16/bf16) = rstd[m] * acc; rstd written by the preceding row kernel
+  // CTA-pair kernel only: the DequantF16 values, re-quantised per row as quantize_symmetric
+  // would quantise the fp16 C (int8 codes through the tmC map, fp32 row scales); C itself is
+  // written only when Params::C is set.
+  DequantQuant = 3,
 };
 
 struct Params {
@@ -69,6 +73,12 @@ struct Params {
   // LK_INJECT_SPLIT_SKIP_PUBLISH  the pair kernel's split-tail writer of leftover tile inj_item,
   //                               warp slot 0, never publishes its partial.
   int inj_kind, inj_block, inj_item;
+  // DequantQuant: the row absmax exchange between the tiles of one row (zeroed by the host
+  // before every launch) and the row scales.
+  uint32_t* q_absmax;  // [M] max |fp16 output| bits of each row, combined with atomicMax
+  int* q_slice_ctr;    // [ceil(M / 32)] tiles that have published their absmax, per 32-row slice
+  float* q_scale;      // [M] scale = absmax / 127
+  uint4* q_park;       // [CTAs][4 warps][2 slots][8 chunks][4][32 lanes] fp16 values of a tile
 };
 constexpr int kMaxScatter = 8;
 

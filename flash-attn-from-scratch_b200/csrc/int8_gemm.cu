@@ -157,8 +157,101 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   return cuda_status((cudaError_t)err);
 }
 
+// Requant workspace layout: [M] row maxima, [ceil(M/32)] slice counters, then (256-byte
+// aligned) the epilogue warps' parking rings, 128 KB per CTA of the largest grid.
+int64_t requant_park_offset(int64_t M) { return ((M + (M + 31) / 32) * 4 + 255) / 256 * 256; }
+int64_t requant_workspace_bytes(int64_t M, int num_sms) {
+  return requant_park_offset(M) + (int64_t)num_sms * 4 * 2 * 1024 * 16;
+}
+
+// The int8 GEMM + dequant whose epilogue also quantises its own fp16 output per row
+// (Epi::DequantQuant on CTA pairs): codes q [M, N] int8 (row pitch ldq) and scales [M], equal
+// bit for bit to quantize_symmetric(C).  C (fp16) is written too when it is not null.
+int run_int8_requant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout, const float* sa,
+                     const float* sb, void* C, int64_t ldc, int8_t* q, int64_t ldq, float* q_scale, uint32_t* ws,
+                     int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return LK_ERR_INVALID_ARG;
+  if (b_layout != 0 && b_layout != 1) return LK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return LK_OK;
+  if (!A || !B || !sa || !sb || !q || !q_scale || !ws || K == 0) return LK_ERR_INVALID_ARG;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return LK_ERR_INVALID_ARG;
+  const bool b_mn = (b_layout == 0);
+  if (lda < K || ldq < N || (C && ldc < N)) return LK_ERR_INVALID_ARG;
+  if (b_mn ? (ldb < N) : (ldb < K)) return LK_ERR_INVALID_ARG;
+  if (lda % 16 || ldb % 16 || ldq % 16 || !aligned16(q)) return LK_ERR_ALIGNMENT;
+  if (int st = bind_stream(stream)) return st;
+  const int num_sms = sm_count();
+  const int ptm = (int)((M + 255) / 256), ptn = (int)((N + 255) / 256);
+  // Every tile of a row block must sit on its own pair, and every pair of the grid must be
+  // resident at once: a tile's epilogue waits for the other tiles of its row block.
+  if (ptn > num_sms / 2) return LK_ERR_UNSUPPORTED;
+  int npairs = 0;
+  {
+    const cudaError_t e = b_mn ? gemm::resident_pairs<Kind::I8, true, Epi::DequantQuant>(num_sms, &npairs)
+                               : gemm::resident_pairs<Kind::I8, false, Epi::DequantQuant>(num_sms, &npairs);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  if (ptn > npairs) return LK_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb, tq;
+  if (int st = make_int8_maps(A, lda, B, ldb, b_mn, (int)M, (int)N, (int)K, 128, &ta, &tb)) return st;
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)ldq};
+    const uint32_t box[2] = {64u, 32u};
+    if (int st = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+  }
+  const int64_t slices = (M + 31) / 32;
+  if (int st = cuda_status(cudaMemsetAsync(ws, 0, (size_t)(M + slices) * sizeof(uint32_t), stream))) return st;
+  // The parking ring follows the counters, 256-byte aligned: 4 warps x 2 slots x 16 KB per CTA.
+  uint4* park = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(ws) + requant_park_offset(M));
+  gemm::Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_m = ptm;
+  p.tiles_n = ptn;
+  p.num_tiles = ptm * ptn;
+  p.full_tiles = p.num_tiles;
+  p.split = 1;
+  p.num_units = p.num_tiles;
+#ifndef LK_REQUANT_GROUP_M
+#define LK_REQUANT_GROUP_M 1
+#endif
+  // Raster groups of g row blocks (N-fastest when g = 1).  A tile's codes are written one
+  // tile after its own pass, once its row block has published; with every row block spread
+  // over fewer than 2 * pairs consecutive tiles those waits only ever point at earlier work.
+  int g = LK_REQUANT_GROUP_M;
+  while (g > 1 && (int64_t)g * ptn > 2 * (int64_t)npairs) --g;
+  p.group_m = g;
+  p.C = C;
+  p.ldc = ldc;
+  p.sa = sa;
+  p.sb = sb;
+  p.c_tma = 1;  // the codes' map
+  p.q_absmax = ws;
+  p.q_slice_ctr = reinterpret_cast<int*>(ws + M);
+  p.q_scale = q_scale;
+  p.q_park = park;
+  const int err = b_mn ? gemm::launch_pair<Kind::I8, true, Epi::DequantQuant>(ta, tb, tq, p, num_sms, stream, npairs)
+                       : gemm::launch_pair<Kind::I8, false, Epi::DequantQuant>(ta, tb, tq, p, num_sms, stream, npairs);
+  return cuda_status((cudaError_t)err);
+}
+
 }  // namespace
 }  // namespace lk
+
+extern "C" int64_t lk_int8_gemm_requant_workspace_bytes(int64_t M) {
+  return M <= 0 ? 0 : lk::requant_workspace_bytes(M, lk::sm_count());
+}
+
+extern "C" int lk_int8_gemm_dequant_requant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                                            const float* scale_a, const float* scale_b, void* C, int64_t ldc,
+                                            int8_t* q, int64_t ldq, float* q_scale, void* workspace, int64_t M,
+                                            int64_t N, int64_t K, void* stream) {
+  return lk::run_int8_requant(A, lda, B, ldb, b_layout, scale_a, scale_b, C, ldc, q, ldq, q_scale,
+                              static_cast<uint32_t*>(workspace), M, N, K, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
                                     const float* scale_a, const float* scale_b, void* C, int64_t ldc, int64_t M,

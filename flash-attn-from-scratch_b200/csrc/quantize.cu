@@ -12,12 +12,18 @@
 // the raw magnitude bits (|x| bit patterns order like the values and every NaN sorts above
 // +inf, so an integer max propagates NaN for free), then codes are produced from the cached
 // registers and written with 4/8-byte stores.  HBM traffic = 1 read of x + 1 write of q.
+// fp16 / bf16 codes come from Markstein's FMA-corrected reciprocal product (quant_common.cuh),
+// which rounds exactly like the IEEE division for every value of those formats (checked
+// exhaustively) -- fp16 inputs put x / scale on a coarse lattice where exact ties are common,
+// so a near-tie test with a division fallback would diverge constantly.  fp32 codes use the
+// reciprocal product with a near-tie test and the IEEE division for the rare near-tie.
 // Rows longer than the register cache take a two-pass path whose second pass is an L2 hit.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "lk_abi.h"
 #include "lk_sm100.cuh"
+#include "quant_common.cuh"
 
 namespace lk {
 namespace {
@@ -106,30 +112,6 @@ __device__ __forceinline__ uint32_t mag_bits<__nv_bfloat16>(__nv_bfloat16 v) {
   return (uint32_t)__bfloat16_as_ushort(v) & 0x7FFFu;
 }
 
-// One code: clamp(rint(x / scale), -128, 127) with NaN -> 0.
-__device__ __forceinline__ int8_t quant_one(float x, float scale) {
-  float t = __fdiv_rn(x, scale);
-  if (t != t) return 0;
-  t = rintf(t);
-  t = fminf(fmaxf(t, -128.0f), 127.0f);
-  return (int8_t)(int)t;
-}
-
-// The row's divisor, with its reciprocal for the fast path.
-struct RowScale {
-  float scale;
-  float rcp;
-  bool fast;  // scale is a positive normal finite number
-};
-
-__device__ __forceinline__ RowScale make_row_scale(float amax) {
-  RowScale s;
-  s.scale = __fdiv_rn(amax, 127.0f);
-  s.fast = (s.scale >= 1.17549435e-38f) && (s.scale < INFINITY);
-  s.rcp = s.fast ? __frcp_rn(s.scale) : 0.f;
-  return s;
-}
-
 // Same code as quant_one, usually without the division.  t = x * rcp differs from the
 // correctly rounded quotient fl(x / scale) by at most 2.3e-5 (|x / scale| <= 127.1: 2^-23
 // relative for the product and reciprocal, half an ulp of 127 for fl), so when t is more
@@ -168,8 +150,7 @@ __device__ __forceinline__ void quant_vec_store<float>(const uint4& v, const Row
   if (bad) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) b[e] = (uint32_t)(uint8_t)quant_one(f[e], s.scale);
-  }
-  *reinterpret_cast<uint32_t*>(q) =
+  }  *reinterpret_cast<uint32_t*>(q) =
       __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
 }
 template <typename T16>
@@ -192,34 +173,17 @@ template <>
 __device__ __forceinline__ float hi16<__nv_bfloat16>(uint32_t w) {
   return __uint_as_float(w & 0xFFFF0000u);
 }
+// fp16 / bf16 vectors: the FMA-corrected quotient of quant_common.cuh (exact for these types,
+// checked exhaustively), so no near-tie test and no per-vector fallback.
 template <typename T16>
 __device__ __forceinline__ void quant_vec16_store(const uint4& v, const RowScale& s, int8_t* q) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float f[8];
+  uint64_t x2[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    f[2 * j] = lo16<T16>(w[j]);
-    f[2 * j + 1] = hi16<T16>(w[j]);
-  }
-  // Branch-free fast path for the whole vector (see quant_code); the exact division only
-  // runs for a vector holding a near-tie or in a row with a non-normal scale.
+  for (int j = 0; j < 4; ++j) x2[j] = f2(lo16<T16>(w[j]), hi16<T16>(w[j]));
   uint32_t b[8];
-  bool bad = !s.fast;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float t = f[e] * s.rcp;
-    const float tb = t + kShift;
-    bad |= !(fabsf(t - (tb - kShift)) <= 0.5f - 2.44140625e-4f);
-    b[e] = __float_as_uint(tb);
-  }
-  if (bad) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) b[e] = (uint32_t)(uint8_t)quant_one(f[e], s.scale);
-  }
-  const uint32_t w0 = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
-  const uint32_t w1 = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
-  *reinterpret_cast<uint2*>(q) = make_uint2(w0, w1);
+  codes_x2<4>(x2, s, b);
+  *reinterpret_cast<uint2*>(q) = make_uint2(pack4_codes(b[0], b[1], b[2], b[3]), pack4_codes(b[4], b[5], b[6], b[7]));
 }
 template <>
 __device__ __forceinline__ void quant_vec_store<__half>(const uint4& v, const RowScale& s, int8_t* q) {

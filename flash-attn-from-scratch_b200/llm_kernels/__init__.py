@@ -26,6 +26,7 @@ from .int8_gemm import (
     int8_gemm_dequant_fwd,
     int8_gemm_dequant_auto,
     int8_gemm_dequant_nk,
+    int8_gemm_dequant_requant,
     int8_gemm_i32,
     quantize_symmetric,
 )

@@ -48,6 +48,10 @@ SIGNATURES = {
     "lk_quantize_symmetric": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "lk_int8_gemm_dequant": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "lk_int8_gemm_i32": (_i, [_p, _i64, _p, _i64, _i, _p, _i64, _i64, _i64, _i64, _p]),
+    "lk_int8_gemm_requant_workspace_bytes": (_i64, [_i64]),
+    "lk_int8_gemm_dequant_requant": (
+        _i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _p],
+    ),
     "lk_int8_gemm_dequant_scatter": (
         _i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _p],
     ),

@@ -6,6 +6,10 @@ Per layer, on x [B, T, d_model]:
                                                                   o is written in [B, T, H, D]
     y   = Int8Linear(d_model, d_model)(o)                        O projection (quantise + int8 GEMM)
     u   = Int8Linear(d_model, d_ff)(y)                           MLP up projection
+The O projection's GEMM also quantises its own output for the MLP-up projection
+(``int8_gemm_dequant_requant``): y goes from the tensor-memory accumulator to int8 codes and
+row scales without an fp16 round trip through HBM and without a separate quantise pass; the
+codes are bit-identical to ``quantize_symmetric(y)``.
 This is the composition the reference's notebook builds from its modules
 (notebooks/dev_walkthrough.ipynb, CustomTransformerBlock) reduced to the ops of the
 benchmark's decoder-layer workload; there is no residual, activation or down projection.
@@ -19,6 +23,7 @@ import torch
 import torch.nn as nn
 
 from .flash_attn import flash_attn_forward
+from .int8_gemm import int8_gemm_dequant_nk, int8_gemm_dequant_requant, quantize_symmetric
 
 __all__ = ["DecoderLayerOps"]
 
@@ -57,10 +62,13 @@ class DecoderLayerOps(nn.Module):
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # [B, H, T, Dh] views
         attn = torch.empty(B, T, H, Dh, dtype=x.dtype, device=x.device)
         flash_attn_forward(q, k, v, causal=True, out=attn.transpose(1, 2))
-        y = self.o_proj(attn.view(B * T, d))
-        u = self.up(y)
+        a_q, a_s = quantize_symmetric(attn.view(B * T, d))
+        res = int8_gemm_dequant_requant(a_q, self.o_proj.w_q, a_s, self.o_proj.scale_w, "nk",
+                                        return_output=return_intermediates)
+        y_q, y_s = res[0], res[1]
+        u = int8_gemm_dequant_nk(y_q, self.up.w_q, y_s, self.up.scale_w)
         if return_intermediates:
-            return u.view(B, T, self.d_ff), {"qkv": qkv, "attn": attn, "y": y}
+            return u.view(B, T, self.d_ff), {"qkv": qkv, "attn": attn, "y": res[2], "y_q": y_q, "y_s": y_s}
         return u.view(B, T, self.d_ff)
 
     def flops(self, B: int, T: int) -> dict:

@@ -23,6 +23,7 @@ __all__ = [
     "int8_gemm_i32",
     "int8_gemm_dequant_nk",
     "int8_gemm_dequant_scatter",
+    "int8_gemm_dequant_requant",
 ]
 
 
@@ -160,6 +161,42 @@ def int8_gemm_dequant_scatter(A, B_nk, scale_a, scale_b, dst_ptrs, ldc: int, col
     dsts = (ctypes.c_void_p * len(dst_ptrs))(*[int(p) for p in dst_ptrs])
     _lib.call("lk_int8_gemm_dequant_scatter", ptr(A), K, ptr(B_nk), K, 1, ptr(scale_a.contiguous()),
               ptr(scale_b.contiguous()), dsts, len(dst_ptrs), ldc, col_offset, M, N, K, stream_for(dev))
+
+
+def int8_gemm_dequant_requant(A, B, scale_a, scale_b, b_layout: str = "nk", return_output: bool = False):
+    """``quantize_symmetric(int8_gemm_dequant(A, B, scale_a, scale_b))`` in one kernel.
+
+    The int8 GEMM's epilogue rounds its dequantised output to fp16 exactly as
+    ``int8_gemm_dequant_fwd`` does and quantises it per row for the next int8 layer, so the
+    fp16 activation need not make a round trip through HBM (the reference ran
+    ``Int8Linear`` -> ``quantize_symmetric`` as separate passes, llm_kernels/__init__.py:111-118).
+    Codes and scales are bit-identical to the two-step result.
+
+    Args:
+        A : [M, K] int8; B : [N, K] int8 (``"nk"``, a weight) or [K, N] (``"kn"``);
+        scale_a : [M] fp32; scale_b : [N] fp32.
+        return_output : also return the fp16 ``C`` (written by the same kernel).
+
+    Returns:
+        (q [M, N] int8, scale [M] fp32), or (q, scale, C) with ``return_output``.
+    """
+    require(b_layout in ("kn", "nk"), "b_layout must be 'kn' or 'nk'")
+    kn = b_layout == "kn"
+    M, N, K = _gemm_checks(A, B, kn_layout=kn)
+    dev = require_cuda("int8_gemm_dequant_requant", A, B, scale_a, scale_b)
+    require(scale_a.dtype == torch.float32 and scale_b.dtype == torch.float32, "scales must be fp32")
+    require(scale_a.numel() == M and scale_b.numel() == N, "scale_a must have M and scale_b N elements")
+    require(K % 16 == 0 and N % 16 == 0, "int8_gemm_dequant_requant: K and N must be multiples of 16")
+    q = torch.empty((M, N), dtype=torch.int8, device=A.device)
+    qs = torch.empty((M,), dtype=torch.float32, device=A.device)
+    C = torch.empty((M, N), dtype=torch.float16, device=A.device) if return_output else None
+    if M and N:
+        lib = _lib.load()
+        ws = torch.empty((int(lib.lk_int8_gemm_requant_workspace_bytes(M)),), dtype=torch.uint8, device=A.device)
+        _lib.call("lk_int8_gemm_dequant_requant", ptr(A), K, ptr(B), B.shape[1], 0 if kn else 1,
+                  ptr(scale_a.contiguous()), ptr(scale_b.contiguous()), ptr(C) if C is not None else None, N,
+                  ptr(q), N, ptr(qs), ptr(ws), M, N, K, stream_for(dev))
+    return (q, qs, C) if return_output else (q, qs)
 
 
 def int8_gemm_i32(A: torch.Tensor, B: torch.Tensor, b_layout: str = "kn") -> torch.Tensor:

@@ -130,6 +130,26 @@ LK_API int lk_int8_gemm_dequant(const int8_t* A, int64_t lda, const int8_t* B, i
                          const float* scale_a, const float* scale_b, void* C, int64_t ldc,
                          int64_t M, int64_t N, int64_t K, void* stream);
 
+/* The same GEMM followed by the next layer's activation quantisation, in one kernel: replaces
+ * the pair `C = int8_gemm_dequant_fwd(...)`; `q, s = quantize_symmetric(C)` of the reference's
+ * int8 linear chain (llm_kernels/__init__.py:111-118 feeding the next Int8Linear), i.e. the
+ * quantise-fused decoder path of notebooks/dev_walkthrough.ipynb:264-337.
+ *     q[m,n], q_scale[m] = quantize_symmetric(C)[m,n]   bit for bit (C as fp16, as above)
+ * The epilogue rounds each output to fp16, the tiles of a row combine their max |C| through
+ * `workspace`, and each tile then writes its codes; C itself is written only when C != NULL.
+ * q is int8 [M,N] row-major, row stride ldq (a multiple of 16, base 16-byte aligned).
+ * workspace: lk_int8_gemm_requant_workspace_bytes(M) bytes of device memory on the current
+ * device, 256-byte aligned (any contents; the call clears what must start at zero on its
+ * stream), not shared with a concurrent call: 4(M + M/32) bytes of row maxima and counters
+ * plus 128 KB per SM where each epilogue warp parks one tile's fp16 values until its row
+ * block's maximum is known (~19 MB on a 148-SM B200).
+ * LK_ERR_UNSUPPORTED when N > 256 * (SM count / 2) (18944 on a 148-SM B200). */
+LK_API int64_t lk_int8_gemm_requant_workspace_bytes(int64_t M);
+LK_API int lk_int8_gemm_dequant_requant(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                                 const float* scale_a, const float* scale_b, void* C, int64_t ldc, int8_t* q,
+                                 int64_t ldq, float* q_scale, void* workspace, int64_t M, int64_t N, int64_t K,
+                                 void* stream);
+
 /* Same GEMM, writing the raw int32 accumulator (C int32 [M,N], row stride ldc) instead of the
  * dequantised fp16.  Exists so the accumulator can be checked bit for bit. */
 LK_API int lk_int8_gemm_i32(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,

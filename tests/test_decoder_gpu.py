@@ -33,8 +33,12 @@ def test_decoder_layer_stagewise_parity():
     aq, sa = oracle.quantize_symmetric(mid["attn"].reshape(B * T, 512).cpu())
     ref_y = oracle.int8_gemm_dequant(aq, layer.o_proj.w_q.cpu().numpy(), sa, layer.o_proj.scale_w.cpu().numpy(), "nk")
     np.testing.assert_array_equal(mid["y"].cpu().numpy().view(np.uint16), ref_y.view(np.uint16))
-    # 4) MLP up projection, bit-exact
+    # 4) the O projection's own re-quantisation of y (fused into its epilogue): codes and
+    #    scales bit-identical to quantize_symmetric(y)
     yq, sy = oracle.quantize_symmetric(mid["y"].cpu())
+    np.testing.assert_array_equal(mid["y_q"].cpu().numpy(), yq)
+    np.testing.assert_array_equal(mid["y_s"].cpu().numpy().view(np.uint32), sy.view(np.uint32))
+    # 5) MLP up projection, bit-exact
     ref_u = oracle.int8_gemm_dequant(yq, layer.up.w_q.cpu().numpy(), sy, layer.up.scale_w.cpu().numpy(), "nk")
     np.testing.assert_array_equal(u.reshape(B * T, 1376).cpu().numpy().view(np.uint16), ref_u.view(np.uint16))
 

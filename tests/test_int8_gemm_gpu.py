@@ -210,3 +210,59 @@ def test_dequant_into_unaligned_output_through_the_c_abi():
         _lib.call("lk_int8_gemm_dequant", ptr(A[:m]), K, ptr(B[:n]), K, 1, ptr(sa[:m]), ptr(sb[:n]), ptr(out), N,
                   m, n, K, stream_for(A.device))
         assert torch.equal(out[:, :n], ref[:m, :n])
+
+
+# GEMM + dequant + re-quantisation of the fp16 output in one kernel (the O projection feeding
+# the next int8 layer): codes and scales must equal quantize_symmetric of the plain GEMM's
+# output bit for bit, C too when it is written.  Shapes: one tile; ragged M and N; N = 11008
+# (43 tiles per row block, rounds that straddle row blocks); config 5's 4096-wide O projection
+# with K = 4096; a few rows only.
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (300, 1008, 256), (1000, 11008, 512), (4096, 4096, 4096),
+                                   (8, 512, 64), (2304, 2304, 1024)])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_requant_epilogue_matches_quantize_of_output(M, N, K, layout):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    A_q, sa = llm_kernels.quantize_symmetric(torch.randn(M, K, generator=g).to(torch.float16).cuda())
+    W_q, sw = llm_kernels.quantize_symmetric(torch.randn(N, K, generator=g).to(torch.float16).cuda())
+    sa = sa * 0.25  # keep |C| well inside fp16 but over several binades
+    B = W_q if layout == "nk" else W_q.T.contiguous()
+    for _ in range(2):  # the second call must not see the first one's row maxima
+        q, s, C = llm_kernels.int8_gemm_dequant_requant(A_q, B, sa, sw, layout, return_output=True)
+    ref_c = oracle.int8_gemm_dequant(A_q.cpu().numpy(), W_q.cpu().numpy(), sa.cpu().numpy(), sw.cpu().numpy(), "nk")
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref_c.view(np.uint16))
+    rq, rs = oracle.quantize_symmetric(torch.from_numpy(ref_c))
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    q2, s2 = llm_kernels.int8_gemm_dequant_requant(A_q, B, sa, sw, layout)
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+    assert llm_kernels.device_status()[0] == 0
+
+
+def test_requant_epilogue_special_rows():
+    """Rows that overflow fp16 (scale inf: codes 0 where the quotient is NaN) and all-zero rows
+    (scale 0, codes 0), as quantize_symmetric treats them."""
+    M, N, K = 512, 768, 128
+    A = _rand_i8((M, K), 21)
+    A[3] = 0
+    A[5] = 127
+    W = _rand_i8((N, K), 22)
+    W[:, :] = W.clamp(min=0)
+    sa = torch.full((M,), 1e-3)
+    sa[5] = 100.0  # row 5: 127 * 127 * K * 100 * sb overflows fp16
+    sw = torch.full((N,), 1e-3)
+    q, s, C = llm_kernels.int8_gemm_dequant_requant(A.cuda(), W.cuda(), sa.cuda(), sw.cuda(), "nk", return_output=True)
+    ref_c = oracle.int8_gemm_dequant(A.numpy(), W.numpy(), sa.numpy(), sw.numpy(), "nk")
+    assert np.isinf(ref_c[5].astype(np.float32)).any()
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint16), ref_c.view(np.uint16))
+    rq, rs = oracle.quantize_symmetric(torch.from_numpy(ref_c))
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+
+
+def test_requant_rejects_too_wide_rows():
+    from llm_kernels._lib import LKError
+
+    A = torch.zeros(256, 64, dtype=torch.int8, device="cuda")
+    W = torch.zeros(256 * 80, 64, dtype=torch.int8, device="cuda")
+    with pytest.raises(LKError):
+        llm_kernels.int8_gemm_dequant_requant(A, W, torch.ones(256, device="cuda"), torch.ones(256 * 80, device="cuda"))
