@@ -407,14 +407,19 @@ def run_ours(args):
     torch.cuda.synchronize()
     del qh, kh, vh, sets, ohs
     decoder = decoder_layer_measure(args, llm_kernels, world, rank, dev)
+    sharded = sharded_gather_measure(args, llm_kernels, world, rank, dev) if world > 1 else None
 
     ops = {}
     cpu = None
     if rank == 0:
-        ops = secondary_ops(args, llm_kernels, peaks)
-        ops["decoder_layer_config5"] = decoder
+        # The metric's other clauses (single-GPU ops) are measured in the 1-GPU run only: at
+        # N > 1 the other ranks would idle at a barrier meanwhile.
         if world == 1:
+            ops = secondary_ops(args, llm_kernels, peaks)
             cpu = cpu_baselines()
+        ops["decoder_layer_config5"] = decoder
+        if sharded is not None:
+            ops["column_sharded_int8_linear"] = sharded
 
     traffic = profile_traffic().get("flash_attn_causal_bf16_B4_H32_N4096_D128")
     # Denominator: the measured cuBLAS bf16 burst peak.  The timed region is a loop of this
@@ -470,6 +475,40 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def sharded_gather_measure(args, llm_kernels, world, rank, dev):
+    """N > 1 only: the column-sharded int8 linear (weight split by output columns, N / g per
+    rank, replicated [M, N] output wanted), with the gather fused into the GEMM epilogue (peer
+    stores over NVLink) against the local GEMM + NCCL all_gather_into_tensor; both include the
+    quantise of x.  Device ms per call, max over ranks; every result is checked equal to the
+    NCCL path's."""
+    from llm_kernels.sharding import (PeerBuffers, column_sharded_int8_linear, column_sharded_int8_linear_fused,
+                                      shard_columns)
+
+    out = {}
+    for M, K, N in ((4096, 4096, 11008), (8192, 4096, 4096)):
+        if N % (8 * world):
+            continue
+        g = torch.Generator().manual_seed(M + N)
+        x = torch.randn(M, K, generator=g).to(torch.float16).to(dev)
+        w = torch.randn(N, K, generator=g).to(torch.float16).to(dev)
+        layer = llm_kernels.Int8Linear(K, N).to(dev)
+        layer.quantize_weights(w)
+        wq = shard_columns(layer.w_q, rank, world).contiguous()
+        sw = shard_columns(layer.scale_w[:, None], rank, world)[:, 0].contiguous()
+        buf = PeerBuffers((M, N))
+        reps = 10
+        ms_f = time_loop(lambda: column_sharded_int8_linear_fused(x, wq, sw, buf), reps, 2, world) / reps
+        ms_n = time_loop(lambda: column_sharded_int8_linear(x, wq, sw, N), reps, 2, world) / reps
+        same = bool(torch.equal(column_sharded_int8_linear_fused(x, wq, sw, buf),
+                                column_sharded_int8_linear(x, wq, sw, N)))
+        buf.close()
+        out[f"M{M}_K{K}_N{N}"] = {"fused_gather_ms": ms_f, "gemm_then_nccl_all_gather_ms": ms_n,
+                                  "speedup": ms_n / ms_f, "bit_identical": same}
+        del x, w, layer, wq, sw, buf
+    torch.cuda.empty_cache()
+    return out
+
+
 def decoder_layer_measure(args, llm_kernels, world, rank, dev):
     """Config 5: the Llama-7B-shaped decoder-layer op mix (RMSNorm+QKV, causal attention,
     int8 O-proj, int8 MLP-up) on a global batch of 64 x 2048 tokens split over the ranks
@@ -495,6 +534,11 @@ def decoder_layer_measure(args, llm_kernels, world, rank, dev):
             "sequences_per_gpu": e - s, "scaling": "strong (global batch 64 x 2048 fixed)"}
 
 
+def roofline_entry(bound, achieved, peak, unit, peak_kind):
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_kind": peak_kind}
+
+
 def secondary_ops(args, llm_kernels, peaks):
     """The metric's other clauses and the rest of the op set (rank 0, L2 flushed per call)."""
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -510,9 +554,12 @@ def secondary_ops(args, llm_kernels, peaks):
     B_q, sb = llm_kernels.quantize_symmetric(B_fp)
     B_kn = B_q.t().contiguous()
     ms = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb), reps, 3, flush)
-    ops["int8_gemm_dequant_4096"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
-                                     "frac_of_4500_dense_int8_spec": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12 / 4500,
-                                     "layout": "B [K,N] (reference API)"}
+    tops = 2 * 4096 ** 3 / (ms * 1e-3) / 1e12
+    ops["int8_gemm_dequant_4096"] = {"value": tops, "unit": "TOPS", "ms": ms,
+                                     "frac_of_4500_dense_int8_spec": tops / 4500,
+                                     "layout": "B [K,N] (reference API)",
+                                     "roofline": roofline_entry("tensor", tops, 4500.0, "TOPS",
+                                                                "dense int8 spec (no measured int8 peak)")}
     ms = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_nk(A_q, B_q, sa, sb), reps, 3, flush)
     ops["int8_gemm_dequant_4096_nk"] = {"value": 2 * 4096 ** 3 / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms": ms,
                                         "layout": "B [N,K] (Int8Linear weight)"}
@@ -529,11 +576,36 @@ def secondary_ops(args, llm_kernels, peaks):
                                             "what": "cuBLASLt int8 x int8 -> int32 via torch._int_mm (comparison)"}
     except Exception as e:  # noqa: BLE001
         ops["vendor_int8_gemm_i32_4096"] = {"unavailable": str(e)[:120]}
+    # The O projection of the decoder layer with its output re-quantised for the MLP-up
+    # projection: one kernel (int8_gemm_dequant_requant) against GEMM + quantize_symmetric.
+    M5 = 131072
+    a5 = torch.randint(-127, 128, (M5, 4096), dtype=torch.int8, device=dev)
+    s5 = torch.rand(M5, device=dev) * 1e-3
+    ms_f = time_each_flushed(lambda: llm_kernels.int8_gemm_dequant_requant(a5, B_q, s5, sb, "nk"), max(3, reps // 4), 2,
+                             flush)
+    ms_2 = time_each_flushed(lambda: llm_kernels.quantize_symmetric(llm_kernels.int8_gemm_dequant_nk(a5, B_q, s5, sb)),
+                             max(3, reps // 4), 2, flush)
+    tops = 2 * M5 * 4096 * 4096 / (ms_f * 1e-3) / 1e12
+    ops["int8_gemm_requant_131072x4096x4096"] = {
+        "value": tops, "unit": "TOPS", "ms": ms_f, "gemm_then_quantize_ms": ms_2,
+        "roofline": roofline_entry("tensor", tops, 4500.0, "TOPS", "dense int8 spec (no measured int8 peak)")}
+    del a5, s5
     # quantize_symmetric 4096x4096 fp16 (config 3b)
     ms = time_each_flushed(lambda: llm_kernels.quantize_symmetric(A_fp), reps, 3, flush)
     qbytes = 4096 * 4096 * 2 + 4096 * 4096 + 4096 * 4
     ops["quantize_4096_f16"] = {"value": qbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ms,
-                                "frac_of_hbm": qbytes / (ms * 1e-3) / 1e9 / hbm}
+                                "frac_of_hbm": qbytes / (ms * 1e-3) / 1e9 / hbm,
+                                "roofline": roofline_entry("hbm", qbytes / (ms * 1e-3) / 1e9, hbm, "GB/s",
+                                                           "measured HBM copy")}
+    # The same quantiser on a config-5 activation (131072 tokens x 4096, bf16, 1 GiB): the size
+    # it runs at inside the decoder layer, where launch and tail costs no longer dominate.
+    xa = torch.randn(131072, 4096, dtype=torch.bfloat16, device=dev)
+    ms = time_each_flushed(lambda: llm_kernels.quantize_symmetric(xa), max(3, reps // 4), 2, flush)
+    qb = 131072 * 4096 * 3 + 131072 * 4
+    ops["quantize_131072x4096_bf16"] = {"value": qb / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ms,
+                                        "roofline": roofline_entry("hbm", qb / (ms * 1e-3) / 1e9, hbm, "GB/s",
+                                                                   "measured HBM copy")}
+    del xa
     # fused RMSNorm + Linear, config 1 shape (bf16 and fp16)
     g = torch.Generator().manual_seed(0)
     x = torch.randn(512, 4096, generator=g)
@@ -543,21 +615,28 @@ def secondary_ops(args, llm_kernels, peaks):
         xd, wnd, wld = x.to(dt).to(dev), wn.to(dt).to(dev), wl.to(dt).to(dev)
         llm_kernels.fused_rmsnorm_linear(xd, wnd, wld)  # folds the weight once (cached per weight version)
         ms = time_each_flushed(lambda: llm_kernels.fused_rmsnorm_linear(xd, wnd, wld), reps, 3, flush)
-        ops[f"rmsnorm_linear_512x4096x4096_{tag}"] = {"value": ms, "unit": "ms",
-                                                      "tflops": 2 * 512 * 4096 * 4096 / (ms * 1e-3) / 1e12}
+        tf = 2 * 512 * 4096 * 4096 / (ms * 1e-3) / 1e12
+        ops[f"rmsnorm_linear_512x4096x4096_{tag}"] = {
+            "value": ms, "unit": "ms", "tflops": tf,
+            "roofline": roofline_entry("tensor", tf, float(peaks["bf16_tflops"]), "TFLOP/s", "measured bf16 burst"),
+            "hbm_frac": 4.195e7 / (ms * 1e-3) / 1e9 / hbm}
     # non-causal FA config 2
     g = torch.Generator().manual_seed(1)
     q = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
     k = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
     v = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev)
     ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, k, v, causal=False), reps, 2, 1) / reps
-    ops["flash_attn_noncausal_bf16_B4H32N4096D128"] = {"value": fa_flops(B, H, N, D, False) / (ms * 1e-3) / 1e12,
-                                                       "unit": "TFLOP/s", "ms": ms}
+    tf = fa_flops(B, H, N, D, False) / (ms * 1e-3) / 1e12
+    ops["flash_attn_noncausal_bf16_B4H32N4096D128"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": ms,
+        "roofline": roofline_entry("tensor", tf, float(peaks["bf16_tflops"]), "TFLOP/s", "measured bf16 burst")}
     # grouped-query attention: 8 K/V heads shared by 32 query heads, read in place
     kg, vg = k[:, :8].contiguous(), v[:, :8].contiguous()
     ms = time_loop(lambda: llm_kernels.flash_attn_forward(q, kg, vg, causal=True), reps, 2, 1) / reps
-    ops["flash_attn_gqa_causal_bf16_B4H32KV8N4096D128"] = {"value": fa_flops(B, H, N, D, True) / (ms * 1e-3) / 1e12,
-                                                           "unit": "TFLOP/s", "ms": ms}
+    tf = fa_flops(B, H, N, D, True) / (ms * 1e-3) / 1e12
+    ops["flash_attn_gqa_causal_bf16_B4H32KV8N4096D128"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": ms,
+        "roofline": roofline_entry("tensor", tf, float(peaks["bf16_tflops"]), "TFLOP/s", "measured bf16 burst")}
     # training path at the config-2 shape: forward with LSE + backward (dQ, dK, dV), causal
     # bf16.  FLOPs counted as the 5 matmuls of the backward (S, dP, dV, dK, dQ: 2.5x the forward),
     # the usual algorithmic count; this implementation runs 7 (its dQ pass recomputes S and dP).
@@ -569,7 +648,9 @@ def secondary_ops(args, llm_kernels, peaks):
     ops["flash_attn_bwd_causal_bf16_B4H32N4096D128"] = {
         "value": 2.5 * FLOPS_CAUSAL / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
         "flops": "2.5x the forward (S, dP, dV, dK, dQ); the kernels execute 3.5x (S and dP recomputed for dQ)",
-        "frac_of_burst": 2.5 * FLOPS_CAUSAL / (ms * 1e-3) / 1e12 / float(peaks["bf16_tflops"])}
+        "frac_of_burst": 2.5 * FLOPS_CAUSAL / (ms * 1e-3) / 1e12 / float(peaks["bf16_tflops"]),
+        "roofline": roofline_entry("tensor", 2.5 * FLOPS_CAUSAL / (ms * 1e-3) / 1e12, float(peaks["bf16_tflops"]),
+                                   "TFLOP/s", "measured bf16 burst")}
     del q, k, v, kg, vg, do, out, lse
     # config 4 sweep: fp16, B8 H16 D64
     sweep = {}
@@ -641,7 +722,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--quick", action="store_true", help="fewer repetitions of the secondary ops")
-    ap.add_argument("--only", choices=["fa", "fa_dense", "fa_bwd", "int8", "quantize", "rmsnorm"], default=None,
+    ap.add_argument("--only", choices=["fa", "fa_dense", "fa_bwd", "int8", "quantize", "quantize_c5", "requant",
+                                       "rmsnorm"], default=None,
                     help="run just one op's device loop (warmup + steps) and print nothing else: "
                          "the command the ncu profiles under profiles/ are taken on")
     args = ap.parse_args()
@@ -681,6 +763,16 @@ def run_only(args):
             fn = lambda: llm_kernels.int8_gemm_dequant_fwd(A_q, B_kn, sa, sb)  # noqa: E731
         else:
             fn = lambda: llm_kernels.quantize_symmetric(A_fp)  # noqa: E731
+    elif args.only == "quantize_c5":
+        xa = torch.randn(131072, 4096, dtype=torch.bfloat16, device=dev)
+        fn = lambda: llm_kernels.quantize_symmetric(xa)  # noqa: E731
+    elif args.only == "requant":
+        # 16384 rows of the O projection (64 row blocks x 16 tiles): a profiling-size case
+        a5 = torch.randint(-127, 128, (16384, 4096), dtype=torch.int8, device=dev)
+        w5 = torch.randint(-127, 128, (4096, 4096), dtype=torch.int8, device=dev)
+        s5 = torch.rand(16384, device=dev) * 1e-3
+        t5 = torch.rand(4096, device=dev) * 1e-3
+        fn = lambda: llm_kernels.int8_gemm_dequant_requant(a5, w5, s5, t5, "nk")  # noqa: E731
     else:
         x = torch.randn(512, 4096, generator=g).to(torch.bfloat16).to(dev)
         wn = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16).to(dev)
