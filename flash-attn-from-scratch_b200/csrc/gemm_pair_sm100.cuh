@@ -502,7 +502,9 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
           const uint32_t mag = max(mag2 & 0xFFFFu, mag2 >> 16);
           if (row_ok) atomicMax(p.q_absmax + m, mag);
           __syncwarp();
-          if (lane == 0) {
+          const bool skip = p.inj_kind == LK_INJECT_REQUANT_SKIP_PUBLISH && p.inj_block == (int)blockIdx.x &&
+                            p.inj_item == local && quad == 0;
+          if (lane == 0 && !skip) {
             __threadfence();  // the warp's maxima are visible before the count that announces them
             atomicAdd(p.q_slice_ctr + (m_warp >> 5), 1);
           }
@@ -751,8 +753,9 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMa
   int pairs = p.num_units < num_sms / 2 ? p.num_units : num_sms / 2;
   if (max_pairs > 0 && pairs > max_pairs) pairs = max_pairs;
   Params pl = p;
-  if (p.split > 1) {
-    const Injection inj = take_injection(LK_INJECT_SPLIT_SKIP_PUBLISH);
+  if (p.split > 1 || kEpi == Epi::DequantQuant) {
+    const Injection inj =
+        take_injection(kEpi == Epi::DequantQuant ? LK_INJECT_REQUANT_SKIP_PUBLISH : LK_INJECT_SPLIT_SKIP_PUBLISH);
     pl.inj_kind = inj.kind;
     pl.inj_block = inj.block;
     pl.inj_item = inj.item;

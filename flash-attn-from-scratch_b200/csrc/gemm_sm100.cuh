@@ -70,6 +70,8 @@ struct Params {
   int num_dst;
   // Test hooks armed by lk_debug_inject (inj_kind 0, the zero-initialised value, = none):
   // LK_INJECT_GEMM_DROP_LOAD  the one-CTA kernel's CTA inj_block skips its inj_item-th stage load;
+  // LK_INJECT_REQUANT_SKIP_PUBLISH  the re-quantising pair kernel: CTA inj_block's quadrant-0
+  //                               epilogue warp does not publish its inj_item-th tile's maxima;
   // LK_INJECT_SPLIT_SKIP_PUBLISH  the pair kernel's split-tail writer of leftover tile inj_item,
   //                               warp slot 0, never publishes its partial.
   int inj_kind, inj_block, inj_item;

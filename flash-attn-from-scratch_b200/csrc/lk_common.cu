@@ -222,7 +222,7 @@ int lk_debug_set_wait_limit(int64_t ns) {
 }
 
 int lk_debug_inject(int kind, int block, int item) {
-  if (kind < LK_INJECT_NONE || kind > LK_INJECT_SPLIT_SKIP_PUBLISH) return LK_ERR_INVALID_ARG;
+  if (kind < LK_INJECT_NONE || kind > LK_INJECT_REQUANT_SKIP_PUBLISH) return LK_ERR_INVALID_ARG;
   if (kind != LK_INJECT_NONE && (block < 0 || item < 0)) return LK_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lock(lk::g_inject_mu);
   lk::g_inject = lk::Injection{kind, block, item};

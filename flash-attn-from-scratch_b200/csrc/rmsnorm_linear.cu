@@ -112,7 +112,23 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   const int nvec = d_in >> 3;
   float ss0 = 0.f, ss1 = 0.f;
   int v = lane;
-  // Two independent accumulators and 4 loads in flight per lane.
+  // Two independent accumulators; 16 loads in flight per lane, so a row of up to 4096 16-bit
+  // values costs one memory round trip (the kernel is latency-bound: few rows, short rows).
+  for (; v + 480 < nvec; v += 512) {
+    uint4 w[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) w[u] = __ldg(xv + v + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      float f[8];
+      unpack8<T>(w[u], f);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        ss0 = fmaf(f[j], f[j], ss0);
+        ss1 = fmaf(f[j + 1], f[j + 1], ss1);
+      }
+    }
+  }
   for (; v + 96 < nvec; v += 128) {
     uint4 w[4];
 #pragma unroll

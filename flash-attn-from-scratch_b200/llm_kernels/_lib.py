@@ -28,6 +28,7 @@ LK_F32, LK_F16, LK_BF16, LK_I8, LK_I32 = 0, 1, 2, 3, 4
 
 # Failure-path test hooks (lk_inject).
 LK_INJECT_NONE, LK_INJECT_FA_DROP_LOAD, LK_INJECT_GEMM_DROP_LOAD, LK_INJECT_SPLIT_SKIP_PUBLISH = 0, 1, 2, 3
+LK_INJECT_REQUANT_SKIP_PUBLISH = 4
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

@@ -85,13 +85,17 @@ LK_API int lk_debug_set_wait_limit(int64_t ns);
  *   LK_INJECT_GEMM_DROP_LOAD      one-CTA GEMM (problems with fewer 256x256 tiles than SM
  *                                 pairs): the producer of CTA `block` skips its `item`-th stage;
  *   LK_INJECT_SPLIT_SKIP_PUBLISH  CTA-pair GEMM split tail: the writer warp of leftover tile
- *                                 `item`, warp slot 0, never publishes its partial.
+ *                                 `item`, warp slot 0, never publishes its partial;
+ *   LK_INJECT_REQUANT_SKIP_PUBLISH  re-quantising GEMM: in CTA `block`, the epilogue warp of
+ *                                 TMEM quadrant 0 never publishes its row maxima for its
+ *                                 `item`-th tile, so that row block's codes warps wait in vain.
  * kind LK_INJECT_NONE disarms. */
 typedef enum {
   LK_INJECT_NONE = 0,
   LK_INJECT_FA_DROP_LOAD = 1,
   LK_INJECT_GEMM_DROP_LOAD = 2,
-  LK_INJECT_SPLIT_SKIP_PUBLISH = 3
+  LK_INJECT_SPLIT_SKIP_PUBLISH = 3,
+  LK_INJECT_REQUANT_SKIP_PUBLISH = 4
 } lk_inject;
 LK_API int lk_debug_inject(int kind, int block, int item);
 

@@ -31,6 +31,7 @@ LIMIT_NS = 20_000_000  # 20 ms: far above any legitimate wait of these tiny laun
 FA_SITES = range(201, 209)     # csrc/flash_attn.cu Site
 GEMM_SITES = range(101, 107)   # csrc/gemm_sm100.cuh Site
 PAIR_SPLIT_SITE = 126          # csrc/gemm_pair_sm100.cuh kSitePairSplit
+PAIR_REQUANT_SITE = 127        # csrc/gemm_pair_sm100.cuh kSitePairRequant
 
 
 @contextlib.contextmanager
@@ -110,3 +111,27 @@ def test_injection_is_one_shot_and_validated():
         assert llm_kernels.device_status()[0] == 0
     finally:
         _lib.call("lk_debug_inject", _lib.LK_INJECT_NONE, 0, 0)
+
+
+def test_requant_unpublished_row_block_times_out_and_recovers():
+    """The re-quantising GEMM's codes warps wait for every tile of their row block to publish its
+    row maxima.  One epilogue warp that never publishes makes that wait run out: the launch
+    reports LK_ERR_TIMEOUT at the requant site and unwinds, and the next call (which clears its
+    workspace itself) is bit-exact again."""
+    M, N, K = 512, 768, 256  # 2 x 3 pair tiles
+    g = torch.Generator().manual_seed(14)
+    A = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8)
+    W = torch.randint(-128, 128, (N, K), generator=g, dtype=torch.int8)
+    sa = torch.rand(M, generator=g) * 1e-3
+    sw = torch.rand(N, generator=g) * 1e-3
+    ref_c = oracle.int8_gemm_dequant(A.numpy(), W.numpy(), sa.numpy(), sw.numpy(), "nk")
+    rq, rs = oracle.quantize_symmetric(torch.from_numpy(ref_c))
+    Ad, Wd, sad, swd = A.cuda(), W.cuda(), sa.cuda(), sw.cuda()
+    with short_waits():
+        _lib.call("lk_debug_inject", _lib.LK_INJECT_REQUANT_SKIP_PUBLISH, 1, 0)
+        llm_kernels.int8_gemm_dequant_requant(Ad, Wd, sad, swd, "nk")
+        _expect_timeout({PAIR_REQUANT_SITE})
+    for _ in range(2):
+        q, s = llm_kernels.int8_gemm_dequant_requant(Ad, Wd, sad, swd, "nk")
+        np.testing.assert_array_equal(q.cpu().numpy(), rq)
+        np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))

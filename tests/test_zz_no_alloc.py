@@ -96,3 +96,8 @@ def test_no_alloc_allocates_nothing_on_the_pair_path():
     ref = _with_scratch(x, w_fold, 1e-6, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert _rel(y, ref) <= REL_TOL
+    # and directly against the fp32 oracle of the reference's op (fused_ops.py:27-37)
+    import oracle
+
+    exact = oracle.rmsnorm_linear_ref(x.float().cpu(), w_norm.float().cpu(), w_lin.float().cpu())
+    assert _rel(y.cpu(), exact) <= REL_TOL
