@@ -481,7 +481,8 @@ def sharded_gather_measure(args, llm_kernels, world, rank, dev):
     stores over NVLink) against the local GEMM + NCCL all_gather_into_tensor; both include the
     quantise of x.  Device ms per call, max over ranks; every result is checked equal to the
     NCCL path's."""
-    from llm_kernels.sharding import (PeerBuffers, column_sharded_int8_linear, column_sharded_int8_linear_fused,
+    from llm_kernels.sharding import (MulticastBuffers, PeerBuffers, column_sharded_int8_linear,
+                                      column_sharded_int8_linear_fused, column_sharded_int8_linear_multicast,
                                       shard_columns)
 
     out = {}
@@ -499,11 +500,25 @@ def sharded_gather_measure(args, llm_kernels, world, rank, dev):
         reps = 10
         ms_f = time_loop(lambda: column_sharded_int8_linear_fused(x, wq, sw, buf), reps, 2, world) / reps
         ms_n = time_loop(lambda: column_sharded_int8_linear(x, wq, sw, N), reps, 2, world) / reps
-        same = bool(torch.equal(column_sharded_int8_linear_fused(x, wq, sw, buf),
-                                column_sharded_int8_linear(x, wq, sw, N)))
+        ref = column_sharded_int8_linear(x, wq, sw, N)
+        same = bool(torch.equal(column_sharded_int8_linear_fused(x, wq, sw, buf), ref))
         buf.close()
-        out[f"M{M}_K{K}_N{N}"] = {"fused_gather_ms": ms_f, "gemm_then_nccl_all_gather_ms": ms_n,
-                                  "speedup": ms_n / ms_f, "bit_identical": same}
+        entry = {"fused_gather_ms": ms_f, "gemm_then_nccl_all_gather_ms": ms_n, "speedup": ms_n / ms_f,
+                 "bit_identical": same}
+        try:
+            mbuf = MulticastBuffers((M, N))
+        except Exception as e:  # noqa: BLE001
+            mbuf = None
+            entry["multicast"] = {"unavailable": str(e)[:100]}
+        if mbuf is not None:
+            ms_m = time_loop(lambda: column_sharded_int8_linear_multicast(x, wq, sw, mbuf), reps, 2, world) / reps
+            y = column_sharded_int8_linear_multicast(x, wq, sw, mbuf)
+            torch.cuda.synchronize()
+            entry["multicast_gather_ms"] = ms_m
+            entry["multicast_speedup_vs_nccl"] = ms_n / ms_m
+            entry["multicast_bit_identical"] = bool(torch.equal(y, ref))
+            mbuf.close()
+        out[f"M{M}_K{K}_N{N}"] = entry
         del x, w, layer, wq, sw, buf
     torch.cuda.empty_cache()
     return out

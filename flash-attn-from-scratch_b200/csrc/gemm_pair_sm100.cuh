@@ -596,8 +596,8 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
               for (int i = 0; i < 4; ++i) {
                 const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
                 if (m_warp + row < p.M)
-                  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 +
-                                            q * 8) = pc[i];
+                  store16_dst(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 + q * 8, pc[i],
+                              p.dst_multimem);
               }
             }
             return;
@@ -679,6 +679,7 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
       __syncwarp();
       if (*(volatile int*)abort_flag) break;
     }
+    if (p.dst_multimem) multimem_release();
     if (lane == 0) bulk_wait_group<0>();  // C stores complete before the CTA's shared memory goes
     __syncwarp();
   }

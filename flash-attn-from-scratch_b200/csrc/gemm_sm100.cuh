@@ -68,6 +68,7 @@ struct Params {
   // buffers mapped into this process over NVLink.
   void* c_dst[8];
   int num_dst;
+  int dst_multimem;  // c_dst[0] (num_dst == 1) is an NVLink multicast address: multimem stores
   // Test hooks armed by lk_debug_inject (inj_kind 0, the zero-initialised value, = none):
   // LK_INJECT_GEMM_DROP_LOAD  the one-CTA kernel's CTA inj_block skips its inj_item-th stage load;
   // LK_INJECT_REQUANT_SKIP_PUBLISH  the re-quantising pair kernel: CTA inj_block's quadrant-0
@@ -241,7 +242,7 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], float row_s
           uint16_t* drow = static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)m * p.ldc + n0;
           if (full_chunk) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(drow)[j] = w[j];
+            for (int j = 0; j < 4; ++j) store16_dst(drow + 8 * j, w[j], p.dst_multimem);
           } else {
             for (int j = 0; j < 32; ++j)
               if (n0 + j < p.N) drow[j] = __half_as_ushort(__float2half_rn(v[j]));
@@ -520,8 +521,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 4; ++i) {
                 const int piece = lane + 32 * i, row = piece >> 2, q = piece & 3;
                 if (m_warp + row < p.M)
-                  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 +
-                                            q * 8) = pc[i];
+                  store16_dst(static_cast<uint16_t*>(p.c_dst[d]) + (int64_t)(m_warp + row) * p.ldc + n0 + q * 8, pc[i],
+                              p.dst_multimem);
               }
             }
             continue;
@@ -532,6 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*(volatile int*)abort_flag) break;
     }
+    if (p.dst_multimem) multimem_release();
   }
 
   tc_fence_before();

@@ -50,7 +50,7 @@ int make_int8_maps(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, b
 template <Epi kEpi>
 int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout, const float* sa,
              const float* sb, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, cudaStream_t stream,
-             void* const* dsts = nullptr, int num_dst = 0) {
+             void* const* dsts = nullptr, int num_dst = 0, int multimem = 0) {
   if (M < 0 || N < 0 || K < 0) return LK_ERR_INVALID_ARG;
   if (b_layout != 0 && b_layout != 1) return LK_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return LK_OK;
@@ -65,9 +65,12 @@ int run_int8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_l
   if (num_dst > 0 && (ldc % 8 || kEpi != Epi::DequantF16 || !aligned16(sb))) return LK_ERR_ALIGNMENT;
   for (int d = 0; d < num_dst; ++d)
     if (!aligned16(dsts[d])) return LK_ERR_ALIGNMENT;
+  // Multicast stores are whole 16-byte vectors of whole 32-column chunks.
+  if (multimem && (num_dst != 1 || N % 32)) return LK_ERR_ALIGNMENT;
   if (int st = bind_stream(stream)) return st;
   auto set_scatter = [&](gemm::Params& p) {
     p.num_dst = num_dst;
+    p.dst_multimem = multimem;
     for (int d = 0; d < num_dst; ++d) p.c_dst[d] = dsts[d];
   };
 
@@ -279,4 +282,15 @@ extern "C" int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const 
   }
   return lk::run_int8<lk::gemm::Epi::DequantF16>(A, lda, B, ldb, b_layout, scale_a, scale_b, at[0], ldc, M, N, K,
                                                  static_cast<cudaStream_t>(stream), at, num_dst);
+}
+
+extern "C" int lk_int8_gemm_dequant_multicast(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                                              int b_layout, const float* scale_a, const float* scale_b,
+                                              void* multicast_dst, int64_t ldc, int64_t col_offset, int64_t M,
+                                              int64_t N, int64_t K, void* stream) {
+  if (!multicast_dst || col_offset < 0 || col_offset % 8) return LK_ERR_INVALID_ARG;
+  if (N > 0 && ldc < col_offset + N) return LK_ERR_INVALID_ARG;
+  void* at[1] = {static_cast<uint16_t*>(multicast_dst) + col_offset};
+  return lk::run_int8<lk::gemm::Epi::DequantF16>(A, lda, B, ldb, b_layout, scale_a, scale_b, at[0], ldc, M, N, K,
+                                                 static_cast<cudaStream_t>(stream), at, 1, 1);
 }

@@ -568,6 +568,27 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 
 
 // ---------------------------------------------------------------------------------------------
+// Stores to another GPU
+// ---------------------------------------------------------------------------------------------
+// 16 bytes of fp16 pairs to a destination that is either an ordinary (local or peer) address
+// or an NVLink multicast address (multimem: one store leaves this GPU and the NVSwitch writes
+// it to every GPU bound to the multicast object).
+__device__ __forceinline__ void store16_dst(void* addr, const uint4& v, int multimem) {
+  if (multimem)
+    asm volatile("multimem.st.weak.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+  else
+    *reinterpret_cast<uint4*>(addr) = v;
+}
+// After the last multicast store of a thread: orders the multicast writes before later
+// accesses through ordinary addresses and makes them visible system-wide.
+__device__ __forceinline__ void multimem_release() {
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
+// ---------------------------------------------------------------------------------------------
 // Misc
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t elect_one() {

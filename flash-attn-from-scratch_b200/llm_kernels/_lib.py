@@ -56,6 +56,9 @@ SIGNATURES = {
     "lk_int8_gemm_dequant_scatter": (
         _i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _p],
     ),
+    "lk_int8_gemm_dequant_multicast": (
+        _i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
+    ),
     "lk_peer_export": (_i, [_i, _p, _p, _pi64]),
     "lk_peer_open": (_i, [_i, _p, _i64, ctypes.POINTER(ctypes.c_void_p)]),
     "lk_peer_close": (_i, [_i, _p, _i64]),

@@ -24,6 +24,7 @@ __all__ = [
     "int8_gemm_dequant_nk",
     "int8_gemm_dequant_scatter",
     "int8_gemm_dequant_requant",
+    "int8_gemm_dequant_multicast",
 ]
 
 
@@ -197,6 +198,28 @@ def int8_gemm_dequant_requant(A, B, scale_a, scale_b, b_layout: str = "nk", retu
                   ptr(scale_a.contiguous()), ptr(scale_b.contiguous()), ptr(C) if C is not None else None, N,
                   ptr(q), N, ptr(qs), ptr(ws), M, N, K, stream_for(dev))
     return (q, qs, C) if return_output else (q, qs)
+
+
+def int8_gemm_dequant_multicast(A, B_nk, scale_a, scale_b, multicast_ptr: int, ldc: int, col_offset: int) -> None:
+    """``int8_gemm_dequant_nk(A, B_nk, ...)`` stored through an NVLink multicast address.
+
+    ``multicast_ptr`` addresses a multicast object bound to every rank's fp16 ``[M, ldc]``
+    output (row pitch ``ldc``); the ``[M, N]`` result goes to columns ``[col_offset,
+    col_offset + N)`` of all of them with one ``multimem`` store per 16 bytes.  N must be a
+    multiple of 32, ``ldc`` and ``col_offset`` multiples of 8, K a multiple of 16.
+    """
+    M, N, K = _gemm_checks(A, B_nk, kn_layout=False)
+    dev = require_cuda("int8_gemm_dequant_multicast", A, B_nk, scale_a, scale_b)
+    require(K % 16 == 0 and N % 32 == 0, "K must be a multiple of 16 and N of 32")
+    require(scale_a.dtype == torch.float32 and scale_b.dtype == torch.float32, "scales must be fp32")
+    require(scale_a.numel() == M and scale_b.numel() == N, "scale_a must have M and scale_b N elements")
+    require(ldc % 8 == 0 and col_offset % 8 == 0 and ldc >= col_offset + N, "ldc/col_offset must be multiples of 8 "
+            "and the block must fit in ldc")
+    require(multicast_ptr != 0 and multicast_ptr % 16 == 0, "multicast_ptr must be a 16-byte aligned address")
+    if M == 0 or N == 0:
+        return
+    _lib.call("lk_int8_gemm_dequant_multicast", ptr(A), K, ptr(B_nk), K, 1, ptr(scale_a.contiguous()),
+              ptr(scale_b.contiguous()), multicast_ptr, ldc, col_offset, M, N, K, stream_for(dev))
 
 
 def int8_gemm_i32(A: torch.Tensor, B: torch.Tensor, b_layout: str = "kn") -> torch.Tensor:

@@ -30,6 +30,8 @@ __all__ = [
     "column_sharded_int8_linear",
     "PeerBuffers",
     "column_sharded_int8_linear_fused",
+    "MulticastBuffers",
+    "column_sharded_int8_linear_multicast",
 ]
 
 
@@ -180,4 +182,65 @@ def column_sharded_int8_linear_fused(x: torch.Tensor, w_q_shard: torch.Tensor, s
     dist.all_reduce(flag, group=group)
     int8_gemm_dequant_scatter(xq, w_q_shard, sx, scale_w_shard, out.ptrs, n_total, s)
     dist.all_reduce(flag, group=group)
+    return out.local
+
+
+class MulticastBuffers:
+    """One ``shape`` fp16 buffer per rank of ``group`` in torch symmetric memory, bound to an
+    NVLink multicast object: a store to ``multicast_ptr`` (a multimem store, issued once by one
+    GPU) is written by the NVSwitch into every rank's buffer.  ``local`` is this rank's buffer.
+
+    Collective: every rank constructs it with the same shape, in the same order.  Raises
+    ``RuntimeError`` where the GPUs have no multicast support (no NVSwitch / NVLS).  ``close()``
+    (collective) before the process group is destroyed."""
+
+    def __init__(self, shape, group=None, dtype=torch.float16):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group = group if group is not None else dist.group.WORLD
+        self.group = group
+        self.world, self.rank = _world(group)
+        self.device = torch.cuda.current_device()
+        self.local = symm_mem.empty(*shape, dtype=dtype, device=f"cuda:{self.device}")
+        self.handle = symm_mem.rendezvous(self.local, group)
+        if not self.handle.multicast_ptr:
+            raise RuntimeError("NVLink multicast is not available on these GPUs")
+        # The tensor's place inside its symmetric allocation, applied to the multicast base.
+        offset = self.local.data_ptr() - self.handle.buffer_ptrs[self.rank]
+        self.multicast_ptr = self.handle.multicast_ptr + offset
+
+    def barrier(self):
+        """Device-side barrier of all ranks on the current stream (symmetric-memory signals)."""
+        self.handle.barrier()
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.handle = None
+        self.local = None
+
+
+def column_sharded_int8_linear_multicast(x: torch.Tensor, w_q_shard: torch.Tensor, scale_w_shard: torch.Tensor,
+                                         out: "MulticastBuffers", group=None) -> torch.Tensor:
+    """``column_sharded_int8_linear`` with the gather done by the NVSwitch: the GEMM epilogue
+    stores each tile of this rank's ``[M, N/g]`` block once to ``out.multicast_ptr`` and the
+    switch replicates it into every rank's ``[M, N_total]`` output, so each rank's block crosses
+    NVLink once (the peer-store path sends it once per peer).  Per-rank column blocks must be
+    multiples of 32 wide and start at multiples of 8.  Returns ``out.local``; a device barrier
+    before the launch keeps a rank from overwriting outputs its peers still read on their
+    current streams, one after it completes once every rank's stores have landed (the same
+    ordering contract as ``column_sharded_int8_linear_fused``)."""
+    from .int8_gemm import int8_gemm_dequant_multicast, quantize_symmetric
+
+    world, rank = _world(group)
+    M, n_total = out.local.shape
+    s, e = shard_range(n_total, rank, world)
+    if w_q_shard.shape[0] != e - s:
+        raise ValueError(f"rank {rank}: weight shard has {w_q_shard.shape[0]} rows, expected {e - s}")
+    if s % 8 or (e - s) % 32:
+        raise ValueError("column blocks must start at multiples of 8 and be multiples of 32 wide")
+    xq, sx = quantize_symmetric(x)
+    out.barrier()
+    int8_gemm_dequant_multicast(xq, w_q_shard, sx, scale_w_shard, out.multicast_ptr, n_total, s)
+    out.barrier()
     return out.local

@@ -175,6 +175,20 @@ LK_API int lk_int8_gemm_dequant_scatter(const int8_t* A, int64_t lda, const int8
                                  const float* scale_a, const float* scale_b, void* const* dsts, int num_dst,
                                  int64_t ldc, int64_t col_offset, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* The same column-sharded layer with the gather done by the NVSwitch: multicast_dst is an
+ * NVLink multicast address (CUDA multicast object, e.g. torch symmetric memory's
+ * multicast_ptr) bound to every rank's replicated [M, N_total] fp16 output, row pitch ldc.
+ * Each epilogue chunk is stored once with multimem.st and the switch writes it to all ranks,
+ * so a rank sends its block over NVLink once instead of once per peer.  Replaces, like
+ * lk_int8_gemm_dequant_scatter, the GEMM + all-gather of a column-split Int8Linear
+ * (llm_kernels/__init__.py:82-121); no counterpart in the reference, which has no
+ * multi-GPU code.  N % 32 == 0, ldc and col_offset multiples of 8, multicast_dst and scale_b
+ * 16-byte aligned.  The caller orders the launch against the outputs' other users on every
+ * rank (a barrier before and after). */
+LK_API int lk_int8_gemm_dequant_multicast(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int b_layout,
+                                   const float* scale_a, const float* scale_b, void* multicast_dst, int64_t ldc,
+                                   int64_t col_offset, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* ---- peer buffers (CUDA IPC) -------------------------------------------------------------- *
  * lk_peer_export writes an LK_PEER_HANDLE_BYTES-byte handle for the allocation holding ptr
  * (on `device`) and ptr's byte offset inside it; another process passes both to lk_peer_open,

@@ -198,10 +198,12 @@ def _worker_fused_gather_gpu(rank, world, port, q):
         dist.init_process_group("nccl", store=store, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=torch.device(f"cuda:{rank}"))
         import llm_kernels
-        from llm_kernels.sharding import PeerBuffers, column_sharded_int8_linear, column_sharded_int8_linear_fused
+        from llm_kernels.sharding import (MulticastBuffers, PeerBuffers, column_sharded_int8_linear,
+                                          column_sharded_int8_linear_fused, column_sharded_int8_linear_multicast)
         from llm_kernels.sharding import shard_columns
 
         results = []
+        multicast_ran, no_mc = False, ""
         for M, K, N in ((1000, 512, 768), (4096, 4096, 4096)):
             g = torch.Generator().manual_seed(M + N)
             x = torch.randn(M, K, generator=g).to(torch.float16).cuda()
@@ -226,8 +228,20 @@ def _worker_fused_gather_gpu(rank, world, port, q):
             y2 = column_sharded_int8_linear_fused(x, wq_r, sw_r, buf2)
             results.append(bool(torch.equal(y2, ref)))
             buf2.close()
+            # The NVSwitch-multicast gather (multimem stores), where the GPUs support it.
+            try:
+                mbuf = MulticastBuffers((M, N))
+            except Exception as e:  # noqa: BLE001  (no NVLS / no symmetric memory here)
+                mbuf, no_mc = None, str(e)[:80]
+            if mbuf is not None:
+                for _ in range(2):
+                    y3 = column_sharded_int8_linear_multicast(x, wq_r, sw_r, mbuf)
+                    torch.cuda.synchronize()
+                    results.append(bool(torch.equal(y3, ref)))
+                mbuf.close()
+                multicast_ran = True
         dist.destroy_process_group()
-        q.put((rank, "ok" if all(results) else f"mismatch {results}"))
+        q.put((rank, ("ok" if multicast_ran else f"ok (no multicast: {no_mc})") if all(results) else f"mismatch {results}"))
     except Exception:
         q.put((rank, traceback.format_exc()))
 
@@ -239,4 +253,5 @@ def test_column_sharded_fused_gather_on_all_gpus():
     (one-CTA kernel) and 2048 / 1024 / 512 columns (CTA-pair kernel at 2 ranks)."""
     world = min(torch.cuda.device_count(), 8)
     out = _run(_worker_fused_gather_gpu, world=world, timeout=300)
-    assert out == {r: "ok" for r in range(world)}, out
+    assert all(v.startswith("ok") for v in out.values()) and len(out) == world, out
+    print("fused gather on", world, "GPUs:", sorted(set(out.values())))
