@@ -722,7 +722,14 @@ def reference_gpu_ops(args, llm_kernels, dev, flush, reps):
     llm_kernels.fused_rmsnorm_linear(x, wn, wl)
     theirs = time_each_flushed(lambda: ref.fused_rmsnorm_linear(x, wn, wl), reps, 3, flush)
     ours = time_each_flushed(lambda: llm_kernels.fused_rmsnorm_linear(x, wn, wl), reps, 3, flush)
-    out["rmsnorm_linear_512x4096x4096_f16"] = {"reference_cuda_ms": theirs, "ours_ms": ours, "speedup": theirs / ours}
+    from kernels.fused_rmsnorm_linear import fused_ops as ref_ops
+    # The reference's CUDA extension builds but does not import (csrc/bindings.cpp:12 declares
+    # launch_fused_rmsnorm_linear with at::Half pointers, csrc/fused_rmsnorm_linear.cu:105 defines
+    # it with half pointers: an undefined symbol), so its dispatcher runs the PyTorch path.
+    out["rmsnorm_linear_512x4096x4096_f16"] = {
+        "reference_ms": theirs, "ours_ms": ours, "speedup": theirs / ours,
+        "reference_path": "CUDA extension" if ref_ops._HAS_CUDA_EXT else
+        "PyTorch fallback (its CUDA extension fails to import: undefined launch_fused_rmsnorm_linear symbol)"}
     xq = torch.randn(4096, 4096, generator=g).to(torch.float16).to(dev)
     theirs = time_each_flushed(lambda: ref.quantize_symmetric(xq), reps, 3, flush)
     ours = time_each_flushed(lambda: llm_kernels.quantize_symmetric(xq), reps, 3, flush)
