@@ -35,10 +35,12 @@ def _inputs(rows, d_in, d_out, dtype, seed):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 # (2304, 1024, 2304), (4100, 512, 4600), (2304, 512, 2300): enough 256 x 256 tiles for the
 # CTA-pair GEMM (the last with an output row pitch that is not a multiple of 16 bytes, so the
-# epilogue stores directly instead of through TMA tiles).
+# epilogue stores directly instead of through TMA tiles).  (300, 2048, 1024), (600, 1024, 2048):
+# the one-CTA kernel with ragged rows.
 @pytest.mark.parametrize("rows,d_in,d_out", [(64, 512, 512), (512, 4096, 4096), (1, 256, 128), (130, 264, 200),
                                              (1000, 1024, 3000), (257, 4096, 384), (2304, 1024, 2304),
-                                             (4100, 512, 4600), (2304, 512, 2300)])
+                                             (4100, 512, 4600), (2304, 512, 2300), (300, 2048, 1024),
+                                             (600, 1024, 2048)])
 def test_matches_fp32_oracle(dtype, rows, d_in, d_out):
     x, wn, wl = _inputs(rows, d_in, d_out, dtype, rows + d_out)
     y = llm_kernels.fused_rmsnorm_linear(x.cuda(), wn.cuda(), wl.cuda(), 1e-6)
