@@ -237,7 +237,8 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
-    if (leader && lane == 0) {
+    // The whole warp runs the loop (voted waits); one elected lane issues each MMA and commit.
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -246,14 +247,14 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
         const Unit w = decode_unit(u, p, num_kb);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
+        if (!mbar_wait_cluster_warp(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kBN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait_cluster(&full[stage], phase, kSitePairFull)) {
+          if (!mbar_wait_cluster_warp(&full[stage], phase, kSitePairFull)) {
             ok = false;
             break;
           }
@@ -269,23 +270,23 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
             else
               bdesc = sdesc_sw128(b_base + ks * 32, 16, 1024);
             if constexpr (kKind == Kind::I8)
-              mma_i8_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
+              mma_i8_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
             else
-              mma_f16_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
+              mma_f16_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
           }
-          tc_commit_pair(cluster_addr(&empty[stage], 0));
-          tc_commit_pair(cluster_addr(&empty[stage], 1));
+          tc_commit_pair_warp(cluster_addr(&empty[stage], 0));
+          tc_commit_pair_warp(cluster_addr(&empty[stage], 1));
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(cluster_addr(&acc_full[acc], 0));
-        tc_commit_pair(cluster_addr(&acc_full[acc], 1));
+        tc_commit_pair_warp(cluster_addr(&acc_full[acc], 0));
+        tc_commit_pair_warp(cluster_addr(&acc_full[acc], 1));
       }
       if (!ok) *(volatile int*)abort_flag = 1;
-      tc_commit_pair(cluster_addr(drain, 0));
+      tc_commit_pair_warp(cluster_addr(drain, 0));
       mbar_wait_drain(drain, 0, kSitePairTeardown);
     }
   } else if (kEpi == Epi::DequantQuant && warp >= 6) {
