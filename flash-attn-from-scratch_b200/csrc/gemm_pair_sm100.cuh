@@ -237,8 +237,23 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
-    // The whole warp runs the loop (voted waits); one elected lane issues each MMA and commit.
-    if (leader) {
+    // The whole warp runs the loop (voted waits) and one elected lane issues each MMA and commit
+    // (7-13% faster than a loop of lane 0 alone), except in the re-quantising epilogue's
+    // kernel, where lane 0 alone measured 3% faster at 131072 rows under the power cap.
+    constexpr bool kWarpIssue = kEpi != Epi::DequantQuant;
+    auto wait_bar = [&](uint64_t* bar, uint32_t parity, int site) {
+      if constexpr (kWarpIssue)
+        return mbar_wait_cluster_warp(bar, parity, site);
+      else
+        return mbar_wait_cluster(bar, parity, site);
+    };
+    auto commit = [&](uint32_t bar_cluster) {
+      if constexpr (kWarpIssue)
+        tc_commit_pair_warp(bar_cluster);
+      else
+        tc_commit_pair(bar_cluster);
+    };
+    if (leader && (kWarpIssue || lane == 0)) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -247,14 +262,14 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
         const Unit w = decode_unit(u, p, num_kb);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_cluster_warp(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
+        if (!wait_bar(&acc_empty[acc], acc_phase ^ 1u, kSitePairAccEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kBN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait_cluster_warp(&full[stage], phase, kSitePairFull)) {
+          if (!wait_bar(&full[stage], phase, kSitePairFull)) {
             ok = false;
             break;
           }
@@ -269,24 +284,29 @@ __global__ void __launch_bounds__(pair_threads(kEpi), 1)
               bdesc = sdesc_sw128(b_base + ks * KT::kMmaK * 128, Cfg::kBBoxBytes, 1024);
             else
               bdesc = sdesc_sw128(b_base + ks * 32, 16, 1024);
-            if constexpr (kKind == Kind::I8)
-              mma_i8_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
+            const uint32_t accumulate = (kb != w.kb0) || (ks != 0);
+            if constexpr (kKind == Kind::I8 && kWarpIssue)
+              mma_i8_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, accumulate);
+            else if constexpr (kKind == Kind::I8)
+              mma_i8_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, accumulate);
+            else if constexpr (kWarpIssue)
+              mma_f16_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, accumulate);
             else
-              mma_f16_ss_pair_warp(d_tmem, adesc, bdesc, Cfg::kIdesc, (kb != w.kb0) || (ks != 0));
+              mma_f16_ss_pair(d_tmem, adesc, bdesc, Cfg::kIdesc, accumulate);
           }
-          tc_commit_pair_warp(cluster_addr(&empty[stage], 0));
-          tc_commit_pair_warp(cluster_addr(&empty[stage], 1));
+          commit(cluster_addr(&empty[stage], 0));
+          commit(cluster_addr(&empty[stage], 1));
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair_warp(cluster_addr(&acc_full[acc], 0));
-        tc_commit_pair_warp(cluster_addr(&acc_full[acc], 1));
+        commit(cluster_addr(&acc_full[acc], 0));
+        commit(cluster_addr(&acc_full[acc], 1));
       }
       if (!ok) *(volatile int*)abort_flag = 1;
-      tc_commit_pair_warp(cluster_addr(drain, 0));
+      commit(cluster_addr(drain, 0));
       mbar_wait_drain(drain, 0, kSitePairTeardown);
     }
   } else if (kEpi == Epi::DequantQuant && warp >= 6) {
