@@ -27,7 +27,7 @@ __device__ __forceinline__ float ex2(float x) {
 // Functions, 1980): x = j + f with j = rint(x) by the 1.5 * 2^23 shifter and |f| <= 1/2 exact;
 // 2^f by a cubic whose coefficients were fitted here by Remez exchange for minimax relative
 // error on [-1/2, 1/2] (7.5e-5, under half an ulp of bf16's 8-bit significand); 2^j is added
-// into the exponent field.  Inputs below -125 (masked keys: -inf) give 2^-125 instead of 0,
+// into the exponent field.  Inputs below -125 (masked keys: -inf) give about 2^-125, not 0,
 // which no bf16 / fp16 P or row sum can tell apart from 0 next to the row maximum's 2^0.
 __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& p0, float& p1) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
