@@ -99,6 +99,16 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append((time.time(), line.strip()))
 
+    def wait_first(self, timeout_s: float = 10.0):
+        """Blocks until nvidia-smi has printed its first sample (its start-up can take seconds
+        on a fresh machine) or `timeout_s` has passed, so the timed window that follows is
+        sampled from its start."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout_s:
+            if self.proc.poll() is not None:
+                break
+            time.sleep(0.01)
+
     def stop(self, window=None):
         """Summary of the samples received inside `window` = (t_start, t_end) host seconds."""
         if self.proc is None:
@@ -335,7 +345,8 @@ def run_ours(args):
         step()
     torch.cuda.synchronize()
     clocks.start()
-    time.sleep(0.5)  # let nvidia-smi start sampling; only samples inside the timed window count
+    clocks.wait_first()  # only samples inside the timed window count
+    time.sleep(0.05)
     t_start = time.time()
     total_ms = time_loop(step, args.steps, 0, world)
     clk = clocks.stop(window=(t_start, time.time()))
